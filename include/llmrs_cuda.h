@@ -1,0 +1,206 @@
+/*
+ * llmrs_cuda.h - C ABI of the B200 (sm_100a) CUDA backend for hedone21/llm.rs.
+ *
+ * This is the drop-in boundary for the batch-1 Llama token loop.  The op-level
+ * entry points replace the methods of the reference's `trait Backend`
+ * (src/backend.rs:15-40) on device-resident f32 buffers; the model-level entry
+ * points replace the per-op token loop of src/core/model.rs:17-49 /
+ * src/core/layer.rs:373-406 with fused, device-resident decode steps (the
+ * reference's OpenCL backend crossed the host/device boundary at every op,
+ * src/backend/opencl.rs:325-345).
+ *
+ * Conventions
+ *   - Every function returns LLMRS_OK (0) or an LLMRS_E* code; the text of the
+ *     last error on the calling thread is available from llmrs_last_error().
+ *     (The reference panics instead, e.g. assert_eq! at src/backend/cpu.rs:37;
+ *     a Rust shim turns a nonzero status back into a panic.)
+ *   - Pointers named d_* (and all op arguments) are device pointers obtained
+ *     from llmrs_malloc; h_* are host pointers owned by the caller.
+ *   - Work is stream-ordered on the context's stream and asynchronous until
+ *     llmrs_d2h / llmrs_sync.  A context is not thread-safe.
+ *   - Q4 weights use the reference's planar layout (src/core/tensor.rs:102-167):
+ *     nibbles [n][k/2] (byte i: element 2i low nibble, 2i+1 high nibble), then
+ *     block scales [n][k/32] as f32 (scale_dtype LLMRS_F32) or as f16 when every
+ *     scale is exactly representable (LLMRS_F16, 18 bytes per 32 weights).
+ *     Q8_0 weights: int8 codes [n][k] and block scales [n][k/32].
+ *     k must be a multiple of 32 (the reference silently drops a k%32 tail,
+ *     src/backend/cpu.rs:665-668; this library rejects it with LLMRS_EINVAL).
+ */
+#ifndef LLMRS_CUDA_H
+#define LLMRS_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+#if defined(__GNUC__)
+#pragma GCC visibility push(default) /* the library builds with -fvisibility=hidden */
+#endif
+
+/* ---- status codes ---- */
+#define LLMRS_OK 0
+#define LLMRS_EINVAL 1     /* bad argument / shape */
+#define LLMRS_ENOMEM 2     /* device allocation failed */
+#define LLMRS_ECUDA 3      /* CUDA runtime/driver error */
+#define LLMRS_ETIMEDOUT 4  /* a bounded device-side wait ran out (peer or pipeline) */
+#define LLMRS_ENOTSUP 5    /* configuration not supported */
+#define LLMRS_ENCCL 6      /* NCCL error */
+#define LLMRS_EDEVICE 7    /* device-side error word set (bad token id, bad position) */
+
+/* ---- dtypes for block scales ---- */
+#define LLMRS_F16 0
+#define LLMRS_F32 1
+
+/* ---- weight formats ---- */
+#define LLMRS_WFMT_Q4_0 0
+#define LLMRS_WFMT_Q8_0 1
+
+typedef struct llmrs_ctx llmrs_ctx;
+typedef struct llmrs_model llmrs_model;
+
+/* ======================================================================
+ * Library / context  (replaces the OpenCL global ProQue + scratch pool,
+ * src/backend/opencl.rs:8-90)
+ * ====================================================================== */
+const char *llmrs_last_error(void);
+const char *llmrs_version(void);
+int llmrs_device_count(int *count);
+int llmrs_ctx_create(int device, llmrs_ctx **out);
+int llmrs_ctx_destroy(llmrs_ctx *ctx);
+/* optional: run on a caller-owned cudaStream_t (NULL restores the context's own stream) */
+int llmrs_ctx_set_stream(llmrs_ctx *ctx, void *cuda_stream);
+int llmrs_malloc(llmrs_ctx *ctx, size_t bytes, void **d_ptr);
+int llmrs_free(llmrs_ctx *ctx, void *d_ptr);
+/* host<->device copies (Tensor::to_device, src/core/tensor.rs:218-291) */
+int llmrs_h2d(llmrs_ctx *ctx, void *d_dst, const void *h_src, size_t bytes);
+int llmrs_d2h(llmrs_ctx *ctx, void *h_dst, const void *d_src, size_t bytes);
+int llmrs_d2d(llmrs_ctx *ctx, void *d_dst, const void *d_src, size_t bytes);
+int llmrs_memset(llmrs_ctx *ctx, void *d_dst, int value, size_t bytes);
+int llmrs_sync(llmrs_ctx *ctx);
+/* Backend::device / Backend::name (src/backend.rs:17-18): "Cuda" and the device ordinal */
+const char *llmrs_backend_name(void);
+int llmrs_ctx_device(llmrs_ctx *ctx, int *device);
+
+/* ======================================================================
+ * Backend trait operations (src/backend.rs:20-39), device f32 buffers
+ * ====================================================================== */
+/* Backend::matmul_transposed, Q4 weights: C[m,n] = A[m,k] . W[n,k]^T with the
+ * Q8_0 activation quantisation of src/backend/cpu.rs:31-111 (per row of A) */
+int llmrs_matmul_transposed_q4(llmrs_ctx *ctx, const float *d_a, const uint8_t *d_qs, const void *d_scales,
+                               int scale_dtype, float *d_c, int m, int k, int n);
+/* same contraction with Q8_0 weights (int8 codes + block scales) */
+int llmrs_matmul_transposed_q8(llmrs_ctx *ctx, const float *d_a, const int8_t *d_qw, const void *d_scales,
+                               int scale_dtype, float *d_c, int m, int k, int n);
+/* Backend::matmul_transposed, f32 weights B[n,k] (src/backend/cpu.rs:113-146) */
+int llmrs_matmul_transposed_f32(llmrs_ctx *ctx, const float *d_a, const float *d_b, float *d_c, int m, int k,
+                                int n);
+/* Backend::matmul: C[m,n] = A[m,k] . B[k,n] (src/backend/cpu.rs:157-224) */
+int llmrs_matmul(llmrs_ctx *ctx, const float *d_a, const float *d_b, float *d_c, int m, int k, int n);
+/* Backend::matmul_slice: C[m,rows] = A[m,cols] . Other[rows,cols]^T (src/backend/cpu.rs:230-269) */
+int llmrs_matmul_slice(llmrs_ctx *ctx, const float *d_a, const float *d_other, float *d_c, int m, int rows,
+                       int cols);
+/* Backend::add_assign: a += b (src/backend/cpu.rs:274-296) */
+int llmrs_add_assign(llmrs_ctx *ctx, float *d_a, const float *d_b, size_t n);
+/* Backend::silu_mul: gate = silu(gate) * up (src/backend/cpu.rs:298-324) */
+int llmrs_silu_mul(llmrs_ctx *ctx, float *d_gate, const float *d_up, size_t n);
+/* Backend::rope_inplace: rotate-half RoPE over rows of head_dim; row i uses
+ * position start_pos + i (src/backend/cpu.rs:326-357; the reference fixes
+ * theta_base = 500000) */
+int llmrs_rope_inplace(llmrs_ctx *ctx, float *d_x, int rows, int head_dim, int start_pos, float theta_base);
+/* Backend::rms_norm (src/backend/cpu.rs:359-393) */
+int llmrs_rms_norm(llmrs_ctx *ctx, const float *d_x, const float *d_w, float *d_y, int rows, int cols,
+                   float eps);
+/* Backend::softmax over the last dimension (src/backend/cpu.rs:395-423) */
+int llmrs_softmax(llmrs_ctx *ctx, const float *d_x, float *d_y, int rows, int cols);
+/* Backend::scale: y = x * value (src/backend/cpu.rs:425-435) */
+int llmrs_scale(llmrs_ctx *ctx, const float *d_x, float *d_y, size_t n, float value);
+/* Backend::copy_from (src/backend/cpu.rs:437-446) */
+int llmrs_copy_from(llmrs_ctx *ctx, const float *d_src, float *d_dst, size_t n);
+
+/* CpuBackend::quantize_row_q8_0 (src/backend/cpu.rs:663-745) for rows of k
+ * values: codes [rows][k] and f32 scales [rows][k/32]; bit-exact */
+int llmrs_quantize_row_q8_0(llmrs_ctx *ctx, const float *d_x, int8_t *d_q, float *d_s, int rows, int k);
+/* Tensor::quantize_q4 (src/core/tensor.rs:102-167): n values -> planar nibbles
+ * [(n+1)/2] and f32 scales [(n+31)/32]; bit-exact */
+int llmrs_quantize_q4(llmrs_ctx *ctx, const float *d_w, size_t n, uint8_t *d_qs, float *d_scales);
+
+/* ======================================================================
+ * Model: device-resident weights + KV cache, fused decode step
+ * (LlamaModel src/core/model.rs, LlamaBlock/Attention/MLP src/core/layer.rs,
+ *  Loader layout decisions src/core/loader.rs:62-198)
+ * ====================================================================== */
+typedef struct {
+    int n_layers, hidden, n_heads, n_kv_heads, head_dim, ffn, vocab;
+    int max_seq;        /* KV capacity (the reference hard-codes 2048, src/core/loader.rs:162-166) */
+    float rms_eps;      /* LlamaConfig::rms_norm_eps */
+    float rope_theta;   /* LlamaConfig::rope_theta (500000) */
+    int weight_format;  /* LLMRS_WFMT_Q4_0 or LLMRS_WFMT_Q8_0 */
+    int tied_embeddings;/* LM head = quantize_q4(embed_tokens), src/core/loader.rs:186-190 */
+    int scale_dtype;    /* LLMRS_F16: 18 B per 32 Q4 weights, every scale must be exactly
+                           representable (synthetic models); LLMRS_F32: the reference's own
+                           f32 scales (20 B per 32), e.g. for quantize_q4 of real checkpoints */
+} llmrs_config;
+
+/* which-codes for llmrs_model_set_weight */
+#define LLMRS_W_Q 0          /* [n_heads*D][hidden]            quantised */
+#define LLMRS_W_K 1          /* [n_kv_heads*D][hidden]         quantised (native GQA, not expanded) */
+#define LLMRS_W_V 2          /* [n_kv_heads*D][hidden]         quantised */
+#define LLMRS_W_O 3          /* [hidden][n_heads*D]            quantised */
+#define LLMRS_W_GATE_UP 4    /* [2*ffn][hidden] gate rows then up rows (src/core/loader.rs:128-147) */
+#define LLMRS_W_DOWN 5       /* [hidden][ffn]                  quantised */
+#define LLMRS_W_ATTN_NORM 6  /* [hidden] f32 */
+#define LLMRS_W_MLP_NORM 7   /* [hidden] f32 */
+#define LLMRS_W_EMBED 8      /* [vocab][hidden] f32 */
+#define LLMRS_W_FINAL_NORM 9 /* [hidden] f32 */
+#define LLMRS_W_LM_HEAD 10   /* [vocab][hidden] quantised (ignored when tied) */
+
+int llmrs_model_create(llmrs_ctx *ctx, const llmrs_config *cfg, llmrs_model **out);
+int llmrs_model_destroy(llmrs_model *model);
+/* random-init every weight from `seed` with the documented synthetic recipe */
+int llmrs_model_init_synthetic(llmrs_model *model, uint64_t seed);
+/* upload one tensor in the reference layout (quantised: h_codes + h_scales as
+ * f32; f32 tensors: h_codes is float*, h_scales NULL).  For the tied 1B head
+ * the LM head is re-derived on the device with quantize_q4 of the embedding. */
+int llmrs_model_set_weight(llmrs_model *model, int layer, int which, const void *h_codes, const float *h_scales);
+/* KV cache: h_k/h_v [n_kv_heads][n_pos][head_dim] f32 written at positions [0,n_pos) */
+int llmrs_kv_fill(llmrs_model *model, int layer, const float *h_k, const float *h_v, int n_pos);
+int llmrs_kv_fill_synthetic(llmrs_model *model, uint64_t seed, int n_pos);
+int llmrs_kv_read(llmrs_model *model, int layer, float *h_k, float *h_v, int n_pos);
+/* one decode step: token at position pos (KV [0,pos) must be valid).  Writes the
+ * next greedy token to *h_argmax and, if h_logits is non-NULL, the [vocab]
+ * logits.  Synchronous. */
+int llmrs_decode_step(llmrs_model *model, int token, int pos, float *h_logits, int *h_argmax);
+/* greedy loop on the device: n_steps decode steps starting from (token, pos),
+ * each step feeding its argmax to the next; tokens_out[i] = argmax of step i.
+ * Runs as CUDA-graph replays with no host round trip between steps. */
+int llmrs_generate(llmrs_model *model, int token, int pos, int n_steps, int *h_tokens_out);
+/* prefill n prompt tokens at positions [start_pos, start_pos+n) (src/main.rs:134-138
+ * chunk, the m>1 path of src/backend/cpu.rs:90-110); writes the last row's
+ * logits / argmax like llmrs_decode_step */
+int llmrs_prefill(llmrs_model *model, const int *h_ids, int n, int start_pos, float *h_logits, int *h_argmax);
+/* read the last decode/prefill logits (device resident) into h_logits[vocab] */
+int llmrs_model_logits(llmrs_model *model, float *h_logits);
+/* host-only helper: the RoPE cos/sin table the decode step uses, [n_pos][head_dim/2]
+ * each, computed with the host libm exactly as src/backend/cpu.rs:345-349 does */
+int llmrs_rope_table(int head_dim, int n_pos, float theta_base, float *h_cos, float *h_sin);
+/* model-level stats: number of kernels the decode step launches */
+int llmrs_model_decode_kernel_count(llmrs_model *model, int *count);
+/* run one decode step kernel by kernel (no graph, no programmatic overlap)
+ * with a CUDA event pair around every kernel on the model's stream; writes
+ * each kernel's duration (ms) to ms_out[i] and its kind to kind_out[i]
+ * (0 QKV GEMV, 1 attention, 2 o_proj GEMV, 3 gate_up GEMV, 4 down GEMV,
+ * 5 LM head GEMV) for i < *n (in: capacity, out: kernels run) */
+int llmrs_model_profile_decode(llmrs_model *model, int token, int pos, float *ms_out, int *kind_out, int *n);
+/* time `iters` device-resident decode steps (graph replays) with CUDA events
+ * on the model's stream; *ms_total = elapsed ms; the KV position advances */
+int llmrs_model_time_decode(llmrs_model *model, int token, int pos, int iters, float *ms_total);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+#ifdef __cplusplus
+}
+#endif
+#endif /* LLMRS_CUDA_H */

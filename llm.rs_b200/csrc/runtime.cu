@@ -1,0 +1,1070 @@
+// runtime.cu - context, device-resident model and the C ABI (include/llmrs_cuda.h).
+//
+// The model keeps every weight in the reference's block formats in one HBM
+// arena (Q4_0 nibbles / Q8_0 codes + block scales), a position-major fp32 KV
+// cache per layer, and a small set of activation buffers.  One decode step is
+// 5 kernels per layer + the LM head (see enqueue_step) and is captured once as
+// a CUDA graph; programmatic dependent launch lets each GEMV start streaming
+// its weights while the previous kernel finishes.
+#include <cuda_fp16.h>
+#include <math.h>
+#include <stdarg.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include <mutex>
+#include <vector>
+
+#include "attention.cuh"
+#include "common.cuh"
+#include "gemv.cuh"
+#include "llmrs_synth.h"
+#include "ops.cuh"
+
+// ------------------------------------------------------------------ errors
+namespace llmrs {
+
+static thread_local char g_err[1024] = "";
+
+void set_error(const char *fmt, ...)
+{
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_err, sizeof(g_err), fmt, ap);
+    va_end(ap);
+}
+
+int fail(int code, const char *fmt, ...)
+{
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_err, sizeof(g_err), fmt, ap);
+    va_end(ap);
+    return code;
+}
+
+int num_sms(int device)
+{
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device) != cudaSuccess || n <= 0)
+        n = 148;
+    return n;
+}
+
+} // namespace llmrs
+
+using namespace llmrs;
+
+struct llmrs_ctx {
+    int device = 0;
+    int sms = 148;
+    cudaStream_t own = nullptr;
+    cudaStream_t stream = nullptr;
+    uint32_t *d_err = nullptr; // op-level device error word
+};
+
+namespace {
+
+struct QW {
+    uint8_t *w = nullptr; // codes
+    void *s = nullptr;    // scales
+    int n = 0, k = 0;
+    int st = 0;           // LLMRS_F16 / LLMRS_F32
+};
+
+struct LayerW {
+    QW qkv, o, gate_up, down;
+    float *attn_norm = nullptr, *mlp_norm = nullptr;
+    float *kc = nullptr, *vc = nullptr;
+};
+
+struct Arena {
+    uint8_t *base = nullptr;
+    size_t size = 0, used = 0;
+    void *take(size_t bytes)
+    {
+        size_t off = (used + 255) & ~size_t(255);
+        if (off + bytes > size)
+            return nullptr;
+        used = off + bytes;
+        return base + off;
+    }
+};
+
+inline size_t wbytes(int wf, size_t n, size_t k) { return wf == 0 ? n * k / 2 : n * k; }
+
+int check_cfg(const llmrs_config *c)
+{
+    LLMRS_CHECK_ARG(c, "config is NULL");
+    LLMRS_CHECK_ARG(c->n_layers > 0 && c->hidden > 0 && c->n_heads > 0 && c->n_kv_heads > 0 && c->head_dim > 0 &&
+                        c->ffn > 0 && c->vocab > 0 && c->max_seq > 0,
+                    "config: all sizes must be positive");
+    LLMRS_CHECK_ARG(c->n_heads % c->n_kv_heads == 0, "config: n_heads %d not a multiple of n_kv_heads %d",
+                    c->n_heads, c->n_kv_heads);
+    LLMRS_CHECK_ARG(c->hidden % 32 == 0 && c->ffn % 32 == 0 && (c->n_heads * c->head_dim) % 32 == 0,
+                    "config: hidden, ffn and n_heads*head_dim must be multiples of 32");
+    LLMRS_CHECK_ARG(c->head_dim == 64 || c->head_dim == 128, "config: head_dim %d not supported (64 or 128)",
+                    c->head_dim);
+    const int nrep = c->n_heads / c->n_kv_heads;
+    LLMRS_CHECK_ARG(nrep == 4 || nrep == 8, "config: n_heads/n_kv_heads = %d not supported (4 or 8)", nrep);
+    LLMRS_CHECK_ARG(c->weight_format == LLMRS_WFMT_Q4_0 || c->weight_format == LLMRS_WFMT_Q8_0,
+                    "config: weight_format %d unknown", c->weight_format);
+    LLMRS_CHECK_ARG(!c->tied_embeddings || c->weight_format == LLMRS_WFMT_Q4_0,
+                    "config: tied embeddings require Q4_0 (quantize_q4 of the embedding)");
+    LLMRS_CHECK_ARG(c->scale_dtype == LLMRS_F16 || c->scale_dtype == LLMRS_F32, "config: scale_dtype %d unknown",
+                    c->scale_dtype);
+    return LLMRS_OK;
+}
+
+} // namespace
+
+struct llmrs_model {
+    llmrs_ctx *ctx = nullptr;
+    llmrs_config cfg{};
+    int wf = 0, st = 0;
+    int D = 0, Hq = 0, Hkv = 0, H = 0, F = 0, V = 0, S = 0;
+    Arena arena;
+    std::vector<LayerW> layers;
+    float *embed = nullptr, *final_norm = nullptr;
+    QW lm_head;
+    float *rope_cos = nullptr, *rope_sin = nullptr;
+    // activations
+    float *x = nullptr, *qkv = nullptr, *ctxv = nullptr, *act = nullptr, *logits = nullptr, *part = nullptr;
+    unsigned int *att_counter = nullptr;
+    StepState *state = nullptr;
+    int *token_log = nullptr;
+    int log_cap = 0;
+    int n_splits = 1;
+    int kernels_per_step = 0;
+    // graph of one decode step
+    cudaGraphExec_t graph = nullptr;
+    // pinned host staging
+    int *h_stage = nullptr; // 13 slots of 4 ints (token, pos) for H2D; [60..61]: next token, err
+    int h_stage_n = 0;
+    uint32_t *d_flag = nullptr;
+};
+
+// ================================================================== C ABI
+extern "C" {
+
+const char *llmrs_last_error(void) { return g_err; }
+
+const char *llmrs_version(void) { return "llmrs-b200 0.1 (sm_100a)"; }
+
+const char *llmrs_backend_name(void) { return "Cuda"; }
+
+int llmrs_device_count(int *count)
+{
+    LLMRS_CHECK_ARG(count, "count is NULL");
+    int n = 0;
+    cudaError_t e = cudaGetDeviceCount(&n);
+    if (e != cudaSuccess) {
+        *count = 0;
+        return fail(LLMRS_ECUDA, "cudaGetDeviceCount: %s", cudaGetErrorString(e));
+    }
+    *count = n;
+    return LLMRS_OK;
+}
+
+int llmrs_ctx_create(int device, llmrs_ctx **out)
+{
+    LLMRS_CHECK_ARG(out, "out is NULL");
+    *out = nullptr;
+    int n = 0;
+    LLMRS_CUDA_TRY(cudaGetDeviceCount(&n));
+    LLMRS_CHECK_ARG(device >= 0 && device < n, "device %d out of range (%d devices)", device, n);
+    LLMRS_CUDA_TRY(cudaSetDevice(device));
+    cudaDeviceProp prop;
+    LLMRS_CUDA_TRY(cudaGetDeviceProperties(&prop, device));
+    if (prop.major != 10)
+        return fail(LLMRS_ENOTSUP, "device %d is sm_%d%d; this library is built for sm_100a (B200)", device,
+                    prop.major, prop.minor);
+    llmrs_ctx *c = new llmrs_ctx();
+    c->device = device;
+    c->sms = num_sms(device);
+    cudaError_t e = cudaStreamCreateWithFlags(&c->own, cudaStreamNonBlocking);
+    if (e == cudaSuccess)
+        e = cudaMalloc(&c->d_err, sizeof(uint32_t));
+    if (e == cudaSuccess)
+        e = cudaMemset(c->d_err, 0, sizeof(uint32_t));
+    if (e != cudaSuccess) {
+        delete c;
+        return fail(LLMRS_ECUDA, "context set-up: %s", cudaGetErrorString(e));
+    }
+    c->stream = c->own;
+    int rc = gemv_prepare();
+    if (rc == LLMRS_OK)
+        rc = attention_prepare();
+    if (rc != LLMRS_OK) {
+        cudaFree(c->d_err);
+        cudaStreamDestroy(c->own);
+        delete c;
+        return rc;
+    }
+    *out = c;
+    return LLMRS_OK;
+}
+
+int llmrs_ctx_destroy(llmrs_ctx *ctx)
+{
+    if (!ctx)
+        return LLMRS_OK;
+    cudaSetDevice(ctx->device);
+    cudaStreamSynchronize(ctx->stream);
+    if (ctx->d_err)
+        cudaFree(ctx->d_err);
+    if (ctx->own)
+        cudaStreamDestroy(ctx->own);
+    delete ctx;
+    return LLMRS_OK;
+}
+
+int llmrs_ctx_set_stream(llmrs_ctx *ctx, void *s)
+{
+    LLMRS_CHECK_ARG(ctx, "ctx is NULL");
+    ctx->stream = s ? reinterpret_cast<cudaStream_t>(s) : ctx->own;
+    return LLMRS_OK;
+}
+
+int llmrs_ctx_device(llmrs_ctx *ctx, int *device)
+{
+    LLMRS_CHECK_ARG(ctx && device, "NULL argument");
+    *device = ctx->device;
+    return LLMRS_OK;
+}
+
+int llmrs_malloc(llmrs_ctx *ctx, size_t bytes, void **d_ptr)
+{
+    LLMRS_CHECK_ARG(ctx && d_ptr, "NULL argument");
+    cudaSetDevice(ctx->device);
+    cudaError_t e = cudaMalloc(d_ptr, bytes ? bytes : 16);
+    if (e != cudaSuccess)
+        return fail(LLMRS_ENOMEM, "cudaMalloc(%zu): %s", bytes, cudaGetErrorString(e));
+    return LLMRS_OK;
+}
+
+int llmrs_free(llmrs_ctx *ctx, void *d_ptr)
+{
+    LLMRS_CHECK_ARG(ctx, "ctx is NULL");
+    if (!d_ptr)
+        return LLMRS_OK;
+    cudaSetDevice(ctx->device);
+    LLMRS_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+    LLMRS_CUDA_TRY(cudaFree(d_ptr));
+    return LLMRS_OK;
+}
+
+int llmrs_h2d(llmrs_ctx *ctx, void *d_dst, const void *h_src, size_t bytes)
+{
+    LLMRS_CHECK_ARG(ctx && (bytes == 0 || (d_dst && h_src)), "NULL argument");
+    LLMRS_CUDA_TRY(cudaMemcpyAsync(d_dst, h_src, bytes, cudaMemcpyHostToDevice, ctx->stream));
+    return LLMRS_OK;
+}
+
+int llmrs_d2h(llmrs_ctx *ctx, void *h_dst, const void *d_src, size_t bytes)
+{
+    LLMRS_CHECK_ARG(ctx && (bytes == 0 || (h_dst && d_src)), "NULL argument");
+    LLMRS_CUDA_TRY(cudaMemcpyAsync(h_dst, d_src, bytes, cudaMemcpyDeviceToHost, ctx->stream));
+    LLMRS_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+    return LLMRS_OK;
+}
+
+int llmrs_d2d(llmrs_ctx *ctx, void *d_dst, const void *d_src, size_t bytes)
+{
+    LLMRS_CHECK_ARG(ctx && (bytes == 0 || (d_dst && d_src)), "NULL argument");
+    LLMRS_CUDA_TRY(cudaMemcpyAsync(d_dst, d_src, bytes, cudaMemcpyDeviceToDevice, ctx->stream));
+    return LLMRS_OK;
+}
+
+int llmrs_memset(llmrs_ctx *ctx, void *d_dst, int value, size_t bytes)
+{
+    LLMRS_CHECK_ARG(ctx && (bytes == 0 || d_dst), "NULL argument");
+    LLMRS_CUDA_TRY(cudaMemsetAsync(d_dst, value, bytes, ctx->stream));
+    return LLMRS_OK;
+}
+
+static int ctx_check_err(llmrs_ctx *ctx)
+{
+    uint32_t e = 0;
+    LLMRS_CUDA_TRY(cudaMemcpy(&e, ctx->d_err, sizeof(e), cudaMemcpyDeviceToHost));
+    if (e) {
+        cudaMemset(ctx->d_err, 0, sizeof(uint32_t));
+        return fail(e == DEV_ERR_MBAR_TIMEOUT || e == DEV_ERR_PEER_TIMEOUT ? LLMRS_ETIMEDOUT : LLMRS_EDEVICE,
+                    "device error word %u", e);
+    }
+    return LLMRS_OK;
+}
+
+int llmrs_sync(llmrs_ctx *ctx)
+{
+    LLMRS_CHECK_ARG(ctx, "ctx is NULL");
+    LLMRS_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+    return ctx_check_err(ctx);
+}
+
+// ---------------------------------------------------------------- ops
+static int gemv_op(llmrs_ctx *ctx, int wf, const float *a, const void *w, const void *scales, int st, float *c,
+                   int m, int k, int n)
+{
+    LLMRS_CHECK_ARG(ctx && a && w && scales && c, "NULL argument");
+    LLMRS_CHECK_ARG(m >= 1 && k >= 32 && k % 32 == 0 && n >= 1, "matmul_transposed: m=%d k=%d n=%d (k must be a multiple of 32)", m, k, n);
+    LLMRS_CHECK_ARG(st == LLMRS_F16 || st == LLMRS_F32, "scale_dtype %d unknown", st);
+    // rows of A are independent (the m>1 path quantises each row, src/backend/cpu.rs:90-110)
+    for (int i = 0; i < m; i++) {
+        GemvParams p{};
+        p.w = reinterpret_cast<const uint8_t *>(w);
+        p.scales = scales;
+        p.N = n;
+        p.K = k;
+        p.x = a + (size_t)i * k;
+        p.y = c + (size_t)i * n;
+        p.err = ctx->d_err;
+        LLMRS_TRY(gemv_launch(p, wf, st, PRO_F32, EPI_STORE, ctx->stream, false, ctx->sms));
+    }
+    return LLMRS_OK;
+}
+
+int llmrs_matmul_transposed_q4(llmrs_ctx *ctx, const float *d_a, const uint8_t *d_qs, const void *d_scales,
+                               int scale_dtype, float *d_c, int m, int k, int n)
+{
+    return gemv_op(ctx, 0, d_a, d_qs, d_scales, scale_dtype, d_c, m, k, n);
+}
+
+int llmrs_matmul_transposed_q8(llmrs_ctx *ctx, const float *d_a, const int8_t *d_qw, const void *d_scales,
+                               int scale_dtype, float *d_c, int m, int k, int n)
+{
+    return gemv_op(ctx, 1, d_a, d_qw, d_scales, scale_dtype, d_c, m, k, n);
+}
+
+int llmrs_matmul_transposed_f32(llmrs_ctx *ctx, const float *d_a, const float *d_b, float *d_c, int m, int k, int n)
+{
+    LLMRS_CHECK_ARG(ctx && d_a && d_b && d_c && m > 0 && k > 0 && n > 0, "matmul_transposed_f32: bad arguments");
+    return op_matmul_t(ctx->stream, d_a, d_b, d_c, m, k, n);
+}
+
+int llmrs_matmul(llmrs_ctx *ctx, const float *d_a, const float *d_b, float *d_c, int m, int k, int n)
+{
+    LLMRS_CHECK_ARG(ctx && d_a && d_b && d_c && m > 0 && k > 0 && n > 0, "matmul: bad arguments");
+    return op_matmul(ctx->stream, d_a, d_b, d_c, m, k, n);
+}
+
+int llmrs_matmul_slice(llmrs_ctx *ctx, const float *d_a, const float *d_other, float *d_c, int m, int rows, int cols)
+{
+    LLMRS_CHECK_ARG(ctx && d_a && d_other && d_c && m > 0 && rows > 0 && cols > 0, "matmul_slice: bad arguments");
+    return op_matmul_t(ctx->stream, d_a, d_other, d_c, m, cols, rows);
+}
+
+int llmrs_add_assign(llmrs_ctx *ctx, float *d_a, const float *d_b, size_t n)
+{
+    LLMRS_CHECK_ARG(ctx && (n == 0 || (d_a && d_b)), "add_assign: bad arguments");
+    return n ? op_add_assign(ctx->stream, d_a, d_b, n) : LLMRS_OK;
+}
+
+int llmrs_silu_mul(llmrs_ctx *ctx, float *d_gate, const float *d_up, size_t n)
+{
+    LLMRS_CHECK_ARG(ctx && (n == 0 || (d_gate && d_up)), "silu_mul: bad arguments");
+    return n ? op_silu_mul(ctx->stream, d_gate, d_up, n) : LLMRS_OK;
+}
+
+int llmrs_rope_inplace(llmrs_ctx *ctx, float *d_x, int rows, int head_dim, int start_pos, float theta_base)
+{
+    LLMRS_CHECK_ARG(ctx && d_x && rows >= 0 && head_dim > 0 && start_pos >= 0, "rope_inplace: bad arguments");
+    return rows ? op_rope(ctx->stream, d_x, rows, head_dim, start_pos, theta_base) : LLMRS_OK;
+}
+
+int llmrs_rms_norm(llmrs_ctx *ctx, const float *d_x, const float *d_w, float *d_y, int rows, int cols, float eps)
+{
+    LLMRS_CHECK_ARG(ctx && d_x && d_w && d_y && rows >= 0 && cols > 0, "rms_norm: bad arguments");
+    return rows ? op_rms_norm(ctx->stream, d_x, d_w, d_y, rows, cols, eps) : LLMRS_OK;
+}
+
+int llmrs_softmax(llmrs_ctx *ctx, const float *d_x, float *d_y, int rows, int cols)
+{
+    LLMRS_CHECK_ARG(ctx && d_x && d_y && rows >= 0 && cols > 0, "softmax: bad arguments");
+    return rows ? op_softmax(ctx->stream, d_x, d_y, rows, cols) : LLMRS_OK;
+}
+
+int llmrs_scale(llmrs_ctx *ctx, const float *d_x, float *d_y, size_t n, float value)
+{
+    LLMRS_CHECK_ARG(ctx && (n == 0 || (d_x && d_y)), "scale: bad arguments");
+    return n ? op_scale(ctx->stream, d_x, d_y, n, value) : LLMRS_OK;
+}
+
+int llmrs_copy_from(llmrs_ctx *ctx, const float *d_src, float *d_dst, size_t n)
+{
+    LLMRS_CHECK_ARG(ctx && (n == 0 || (d_src && d_dst)), "copy_from: bad arguments");
+    return n ? op_copy(ctx->stream, d_src, d_dst, n) : LLMRS_OK;
+}
+
+int llmrs_quantize_row_q8_0(llmrs_ctx *ctx, const float *d_x, int8_t *d_q, float *d_s, int rows, int k)
+{
+    LLMRS_CHECK_ARG(ctx && d_x && d_q && d_s && rows >= 0 && k > 0 && k % 32 == 0,
+                    "quantize_row_q8_0: bad arguments (k=%d must be a multiple of 32)", k);
+    return op_quantize_q8(ctx->stream, d_x, d_q, d_s, (size_t)rows * (k / 32));
+}
+
+int llmrs_quantize_q4(llmrs_ctx *ctx, const float *d_w, size_t n, uint8_t *d_qs, float *d_scales)
+{
+    LLMRS_CHECK_ARG(ctx && (n == 0 || (d_w && d_qs && d_scales)), "quantize_q4: bad arguments");
+    return op_quantize_q4(ctx->stream, d_w, n, d_qs, d_scales);
+}
+
+// ---------------------------------------------------------------- model
+int llmrs_rope_table(int head_dim, int n_pos, float theta_base, float *h_cos, float *h_sin)
+{
+    LLMRS_CHECK_ARG(head_dim > 0 && head_dim % 2 == 0 && n_pos >= 0 && h_cos && h_sin, "rope_table: bad arguments");
+    const int mid = head_dim / 2;
+    for (int pos = 0; pos < n_pos; pos++)
+        for (int j = 0; j < mid; j++) {
+            // src/backend/cpu.rs:346-349, each operation rounded to f32
+            volatile float freq_idx = ((float)j * 2.0f) / (float)head_dim;
+            volatile float theta = 1.0f / powf(theta_base, freq_idx);
+            volatile float m_theta = (float)pos * theta;
+            h_sin[(size_t)pos * mid + j] = sinf(m_theta);
+            h_cos[(size_t)pos * mid + j] = cosf(m_theta);
+        }
+    return LLMRS_OK;
+}
+
+static void model_free(llmrs_model *m)
+{
+    if (!m)
+        return;
+    if (m->graph)
+        cudaGraphExecDestroy(m->graph);
+    if (m->arena.base)
+        cudaFree(m->arena.base);
+    if (m->h_stage)
+        cudaFreeHost(m->h_stage);
+    delete m;
+}
+
+int llmrs_model_create(llmrs_ctx *ctx, const llmrs_config *cfg, llmrs_model **out)
+{
+    LLMRS_CHECK_ARG(ctx && out, "NULL argument");
+    *out = nullptr;
+    LLMRS_TRY(check_cfg(cfg));
+    LLMRS_CUDA_TRY(cudaSetDevice(ctx->device));
+    llmrs_model *m = new llmrs_model();
+    m->ctx = ctx;
+    m->cfg = *cfg;
+    m->wf = cfg->weight_format;
+    m->st = cfg->scale_dtype;
+    m->D = cfg->head_dim;
+    m->Hq = cfg->n_heads;
+    m->Hkv = cfg->n_kv_heads;
+    m->H = cfg->hidden;
+    m->F = cfg->ffn;
+    m->V = cfg->vocab;
+    m->S = cfg->max_seq;
+    m->n_splits = attention_default_splits(m->Hkv);
+    m->log_cap = 1 << 16;
+    const int D = m->D, H = m->H, F = m->F, V = m->V, S = m->S;
+    const size_t qkv_rows = (size_t)(m->Hq + 2 * m->Hkv) * D;
+    const size_t qdim = (size_t)m->Hq * D;
+    const int wf = m->wf;
+    // arena size (scales always reserve 4 bytes so either dtype fits)
+    auto qsize = [&](size_t n, size_t k) { return wbytes(wf, n, k) + n * k / 32 * 4 + 512; };
+    size_t total = 0;
+    for (int l = 0; l < cfg->n_layers; l++) {
+        total += qsize(qkv_rows, H) + qsize(H, qdim) + qsize(2 * (size_t)F, H) + qsize(H, F);
+        total += 2 * (size_t)H * 4 + 512;
+        total += 2 * (size_t)m->Hkv * S * D * 4 + 512;
+    }
+    total += (size_t)V * H * 4 + 256;                                       // embed
+    total += (size_t)H * 4 + 256;                                           // final norm
+    total += (cfg->tied_embeddings ? (size_t)V * H / 2 : wbytes(wf, V, H)) + (size_t)V * H / 32 * 4 + 512;
+    total += 2 * (size_t)S * D / 2 * 4 + 512;                              // rope
+    total += ((size_t)H + qkv_rows + qdim + F + V) * 4 + 5 * 256;           // activations
+    total += attention_partials_floats(m->Hq, D, m->n_splits) * 4 + 256;
+    total += (size_t)m->Hkv * 4 + sizeof(StepState) + (size_t)m->log_cap * 4 + 1024;
+    cudaError_t e = cudaMalloc(&m->arena.base, total);
+    if (e != cudaSuccess) {
+        model_free(m);
+        return fail(LLMRS_ENOMEM, "model arena of %zu bytes: %s", total, cudaGetErrorString(e));
+    }
+    m->arena.size = total;
+    Arena &A = m->arena;
+    auto mkq = [&](QW &q, size_t n, size_t k, int st) {
+        q.n = (int)n;
+        q.k = (int)k;
+        q.st = st;
+        q.w = (uint8_t *)A.take(wbytes(wf, n, k));
+        q.s = A.take(n * k / 32 * 4);
+    };
+    m->layers.resize(cfg->n_layers);
+    for (auto &L : m->layers) {
+        mkq(L.qkv, qkv_rows, H, m->st);
+        mkq(L.o, H, qdim, m->st);
+        mkq(L.gate_up, 2 * (size_t)F, H, m->st);
+        mkq(L.down, H, F, m->st);
+        L.attn_norm = (float *)A.take((size_t)H * 4);
+        L.mlp_norm = (float *)A.take((size_t)H * 4);
+        L.kc = (float *)A.take((size_t)m->Hkv * S * D * 4);
+        L.vc = (float *)A.take((size_t)m->Hkv * S * D * 4);
+    }
+    m->embed = (float *)A.take((size_t)V * H * 4);
+    m->final_norm = (float *)A.take((size_t)H * 4);
+    if (cfg->tied_embeddings) {
+        m->lm_head.n = V;
+        m->lm_head.k = H;
+        m->lm_head.st = LLMRS_F32;
+        m->lm_head.w = (uint8_t *)A.take((size_t)V * H / 2);
+        m->lm_head.s = A.take((size_t)V * H / 32 * 4);
+    } else {
+        mkq(m->lm_head, V, H, m->st);
+    }
+    m->rope_cos = (float *)A.take((size_t)S * D / 2 * 4);
+    m->rope_sin = (float *)A.take((size_t)S * D / 2 * 4);
+    m->x = (float *)A.take((size_t)H * 4);
+    m->qkv = (float *)A.take(qkv_rows * 4);
+    m->ctxv = (float *)A.take(qdim * 4);
+    m->act = (float *)A.take((size_t)F * 4);
+    m->logits = (float *)A.take((size_t)V * 4);
+    m->part = (float *)A.take(attention_partials_floats(m->Hq, D, m->n_splits) * 4);
+    m->att_counter = (unsigned int *)A.take((size_t)m->Hkv * 4);
+    m->state = (StepState *)A.take(sizeof(StepState));
+    m->token_log = (int *)A.take((size_t)m->log_cap * 4);
+    if (!m->token_log) {
+        model_free(m);
+        return fail(LLMRS_ENOMEM, "model arena layout overflow");
+    }
+    cudaStream_t s = ctx->stream;
+    e = cudaMemsetAsync(m->arena.base, 0, total, s);
+    // RoPE table from the host libm (bit-exact with the reference)
+    std::vector<float> hc((size_t)S * D / 2), hs((size_t)S * D / 2);
+    llmrs_rope_table(D, S, cfg->rope_theta, hc.data(), hs.data());
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(m->rope_cos, hc.data(), hc.size() * 4, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(m->rope_sin, hs.data(), hs.size() * 4, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess)
+        e = cudaHostAlloc((void **)&m->h_stage, 64 * sizeof(int), cudaHostAllocDefault);
+    if (e == cudaSuccess) {
+        StepState st0{};
+        st0.log_cap = m->log_cap;
+        e = cudaMemcpyAsync(m->state, &st0, sizeof(st0), cudaMemcpyHostToDevice, s);
+    }
+    if (e == cudaSuccess)
+        e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) {
+        model_free(m);
+        return fail(LLMRS_ECUDA, "model set-up: %s", cudaGetErrorString(e));
+    }
+    m->kernels_per_step = 5 * cfg->n_layers + 1;
+    *out = m;
+    return LLMRS_OK;
+}
+
+int llmrs_model_destroy(llmrs_model *m)
+{
+    if (!m)
+        return LLMRS_OK;
+    cudaSetDevice(m->ctx->device);
+    cudaStreamSynchronize(m->ctx->stream);
+    model_free(m);
+    return LLMRS_OK;
+}
+
+static int finish_sync(llmrs_model *m)
+{
+    LLMRS_CUDA_TRY(cudaStreamSynchronize(m->ctx->stream));
+    return LLMRS_OK;
+}
+
+int llmrs_model_init_synthetic(llmrs_model *m, uint64_t seed)
+{
+    LLMRS_CHECK_ARG(m, "model is NULL");
+    LLMRS_CHECK_ARG(m->st == LLMRS_F16 || m->st == LLMRS_F32, "bad scale dtype");
+    cudaSetDevice(m->ctx->device);
+    cudaStream_t s = m->ctx->stream;
+    const int D = m->D, H = m->H, F = m->F, V = m->V;
+    const int qd = m->Hq * D, kd = m->Hkv * D;
+    for (int l = 0; l < m->cfg.n_layers; l++) {
+        LayerW &L = m->layers[l];
+        // fused QKV rows: q | k | v (native GQA)
+        LLMRS_TRY(synth_quant(s, m->wf, seed, l, LLMRS_T_Q, H, 0, qd, 0, H, L.qkv.w, L.qkv.s, L.qkv.st, 1, 0));
+        LLMRS_TRY(synth_quant(s, m->wf, seed, l, LLMRS_T_K, H, 0, kd, 0, H, L.qkv.w, L.qkv.s, L.qkv.st, 1, qd));
+        LLMRS_TRY(synth_quant(s, m->wf, seed, l, LLMRS_T_V, H, 0, kd, 0, H, L.qkv.w, L.qkv.s, L.qkv.st, 1, qd + kd));
+        LLMRS_TRY(synth_quant(s, m->wf, seed, l, LLMRS_T_O, qd, 0, H, 0, qd, L.o.w, L.o.s, L.o.st, 1, 0));
+        // gate/up interleaved: device row 2i = gate i, 2i+1 = up i
+        LLMRS_TRY(synth_quant(s, m->wf, seed, l, LLMRS_T_GATE, H, 0, F, 0, H, L.gate_up.w, L.gate_up.s, L.gate_up.st, 2, 0));
+        LLMRS_TRY(synth_quant(s, m->wf, seed, l, LLMRS_T_UP, H, 0, F, 0, H, L.gate_up.w, L.gate_up.s, L.gate_up.st, 2, 1));
+        LLMRS_TRY(synth_quant(s, m->wf, seed, l, LLMRS_T_DOWN, F, 0, H, 0, F, L.down.w, L.down.s, L.down.st, 1, 0));
+        LLMRS_TRY(synth_normal(s, seed, l, LLMRS_T_ATTN_NORM, H, 1.0f, 0.02f, L.attn_norm));
+        LLMRS_TRY(synth_normal(s, seed, l, LLMRS_T_MLP_NORM, H, 1.0f, 0.02f, L.mlp_norm));
+    }
+    LLMRS_TRY(synth_normal(s, seed, LLMRS_GLOBAL_LAYER, LLMRS_T_EMBED, (size_t)V * H, 1.0f, 0.02f, m->embed));
+    LLMRS_TRY(synth_normal(s, seed, LLMRS_GLOBAL_LAYER, LLMRS_T_FINAL_NORM, H, 1.0f, 0.02f, m->final_norm));
+    if (m->cfg.tied_embeddings)
+        LLMRS_TRY(op_quantize_q4(s, m->embed, (size_t)V * H, m->lm_head.w, (float *)m->lm_head.s));
+    else
+        LLMRS_TRY(synth_quant(s, m->wf, seed, LLMRS_GLOBAL_LAYER, LLMRS_T_LM_HEAD, H, 0, V, 0, H, m->lm_head.w,
+                              m->lm_head.s, m->lm_head.st, 1, 0));
+    return finish_sync(m);
+}
+
+// upload n rows of a quantised tensor (reference layout) into dst rows
+// row*mul + add of a device tensor with the same k
+static int upload_quant(llmrs_model *m, const QW &q, const void *h_codes, const float *h_scales, size_t n, size_t k,
+                        int mul, int add)
+{
+    cudaStream_t s = m->ctx->stream;
+    const size_t rb = m->wf == 0 ? k / 2 : k;
+    const size_t nb = k / 32;
+    LLMRS_CUDA_TRY(cudaMemcpy2DAsync(q.w + (size_t)add * rb, rb * mul, h_codes, rb, rb, n, cudaMemcpyHostToDevice, s));
+    if (q.st == LLMRS_F32) {
+        LLMRS_CUDA_TRY(cudaMemcpy2DAsync((uint8_t *)q.s + (size_t)add * nb * 4, nb * 4 * mul, h_scales, nb * 4,
+                                         nb * 4, n, cudaMemcpyHostToDevice, s));
+        return LLMRS_OK;
+    }
+    // f16 storage: stage the f32 scales, convert on device, check exactness
+    float *tmp = nullptr;
+    LLMRS_CUDA_TRY(cudaMallocAsync((void **)&tmp, n * nb * 4 + 16, s));
+    LLMRS_CUDA_TRY(cudaMemcpyAsync(tmp, h_scales, n * nb * 4, cudaMemcpyHostToDevice, s));
+    uint32_t *flag = m->ctx->d_err; // reuse the op error word as the inexact flag
+    LLMRS_CUDA_TRY(cudaMemsetAsync(flag, 0, 4, s));
+    __half *h16 = nullptr;
+    LLMRS_CUDA_TRY(cudaMallocAsync((void **)&h16, n * nb * 2 + 16, s));
+    LLMRS_TRY(scales_to_f16(s, tmp, h16, n * nb, flag));
+    LLMRS_CUDA_TRY(cudaMemcpy2DAsync((uint8_t *)q.s + (size_t)add * nb * 2, nb * 2 * mul, h16, nb * 2, nb * 2, n,
+                                     cudaMemcpyDeviceToDevice, s));
+    LLMRS_CUDA_TRY(cudaFreeAsync(tmp, s));
+    LLMRS_CUDA_TRY(cudaFreeAsync(h16, s));
+    uint32_t inexact = 0;
+    LLMRS_CUDA_TRY(cudaMemcpyAsync(&inexact, flag, 4, cudaMemcpyDeviceToHost, s));
+    LLMRS_CUDA_TRY(cudaStreamSynchronize(s));
+    LLMRS_CUDA_TRY(cudaMemsetAsync(flag, 0, 4, s));
+    if (inexact)
+        return fail(LLMRS_EINVAL, "a block scale is not exactly representable in f16; create the model with "
+                                  "scale_dtype = LLMRS_F32");
+    return LLMRS_OK;
+}
+
+int llmrs_model_set_weight(llmrs_model *m, int layer, int which, const void *h_codes, const float *h_scales)
+{
+    LLMRS_CHECK_ARG(m && h_codes, "NULL argument");
+    cudaSetDevice(m->ctx->device);
+    cudaStream_t s = m->ctx->stream;
+    const int D = m->D, H = m->H, F = m->F, V = m->V;
+    const size_t qd = (size_t)m->Hq * D, kd = (size_t)m->Hkv * D;
+    const bool global = which == LLMRS_W_EMBED || which == LLMRS_W_FINAL_NORM || which == LLMRS_W_LM_HEAD;
+    LLMRS_CHECK_ARG(global || (layer >= 0 && layer < m->cfg.n_layers), "layer %d out of range", layer);
+    const bool quant = which <= LLMRS_W_DOWN || which == LLMRS_W_LM_HEAD;
+    LLMRS_CHECK_ARG(!quant || h_scales, "quantised tensor needs scales");
+    switch (which) {
+    case LLMRS_W_Q: LLMRS_TRY(upload_quant(m, m->layers[layer].qkv, h_codes, h_scales, qd, H, 1, 0)); break;
+    case LLMRS_W_K: LLMRS_TRY(upload_quant(m, m->layers[layer].qkv, h_codes, h_scales, kd, H, 1, (int)qd)); break;
+    case LLMRS_W_V: LLMRS_TRY(upload_quant(m, m->layers[layer].qkv, h_codes, h_scales, kd, H, 1, (int)(qd + kd))); break;
+    case LLMRS_W_O: LLMRS_TRY(upload_quant(m, m->layers[layer].o, h_codes, h_scales, H, qd, 1, 0)); break;
+    case LLMRS_W_GATE_UP: {
+        // reference layout: gate rows [0,F), then up rows [F,2F) -> interleave
+        const size_t rb = m->wf == 0 ? (size_t)H / 2 : (size_t)H;
+        const uint8_t *c = (const uint8_t *)h_codes;
+        LLMRS_TRY(upload_quant(m, m->layers[layer].gate_up, c, h_scales, F, H, 2, 0));
+        LLMRS_TRY(upload_quant(m, m->layers[layer].gate_up, c + (size_t)F * rb, h_scales + (size_t)F * (H / 32), F, H, 2, 1));
+        break;
+    }
+    case LLMRS_W_DOWN: LLMRS_TRY(upload_quant(m, m->layers[layer].down, h_codes, h_scales, H, F, 1, 0)); break;
+    case LLMRS_W_ATTN_NORM:
+        LLMRS_CUDA_TRY(cudaMemcpyAsync(m->layers[layer].attn_norm, h_codes, (size_t)H * 4, cudaMemcpyHostToDevice, s));
+        break;
+    case LLMRS_W_MLP_NORM:
+        LLMRS_CUDA_TRY(cudaMemcpyAsync(m->layers[layer].mlp_norm, h_codes, (size_t)H * 4, cudaMemcpyHostToDevice, s));
+        break;
+    case LLMRS_W_EMBED:
+        LLMRS_CUDA_TRY(cudaMemcpyAsync(m->embed, h_codes, (size_t)V * H * 4, cudaMemcpyHostToDevice, s));
+        if (m->cfg.tied_embeddings) // src/core/loader.rs:186-190
+            LLMRS_TRY(op_quantize_q4(s, m->embed, (size_t)V * H, m->lm_head.w, (float *)m->lm_head.s));
+        break;
+    case LLMRS_W_FINAL_NORM:
+        LLMRS_CUDA_TRY(cudaMemcpyAsync(m->final_norm, h_codes, (size_t)H * 4, cudaMemcpyHostToDevice, s));
+        break;
+    case LLMRS_W_LM_HEAD:
+        if (m->cfg.tied_embeddings)
+            return LLMRS_OK; // derived from the embedding
+        LLMRS_TRY(upload_quant(m, m->lm_head, h_codes, h_scales, V, H, 1, 0));
+        break;
+    default:
+        return fail(LLMRS_EINVAL, "unknown weight id %d", which);
+    }
+    return finish_sync(m);
+}
+
+int llmrs_kv_fill(llmrs_model *m, int layer, const float *h_k, const float *h_v, int n_pos)
+{
+    LLMRS_CHECK_ARG(m && h_k && h_v, "NULL argument");
+    LLMRS_CHECK_ARG(layer >= 0 && layer < m->cfg.n_layers, "layer %d out of range", layer);
+    LLMRS_CHECK_ARG(n_pos >= 0 && n_pos <= m->S, "n_pos %d exceeds max_seq %d", n_pos, m->S);
+    if (n_pos == 0)
+        return LLMRS_OK;
+    cudaSetDevice(m->ctx->device);
+    const size_t row = (size_t)n_pos * m->D * 4, pitch = (size_t)m->S * m->D * 4;
+    cudaStream_t s = m->ctx->stream;
+    LLMRS_CUDA_TRY(cudaMemcpy2DAsync(m->layers[layer].kc, pitch, h_k, row, row, m->Hkv, cudaMemcpyHostToDevice, s));
+    LLMRS_CUDA_TRY(cudaMemcpy2DAsync(m->layers[layer].vc, pitch, h_v, row, row, m->Hkv, cudaMemcpyHostToDevice, s));
+    return finish_sync(m);
+}
+
+int llmrs_kv_read(llmrs_model *m, int layer, float *h_k, float *h_v, int n_pos)
+{
+    LLMRS_CHECK_ARG(m && h_k && h_v, "NULL argument");
+    LLMRS_CHECK_ARG(layer >= 0 && layer < m->cfg.n_layers, "layer %d out of range", layer);
+    LLMRS_CHECK_ARG(n_pos >= 0 && n_pos <= m->S, "n_pos %d exceeds max_seq %d", n_pos, m->S);
+    if (n_pos == 0)
+        return LLMRS_OK;
+    cudaSetDevice(m->ctx->device);
+    const size_t row = (size_t)n_pos * m->D * 4, pitch = (size_t)m->S * m->D * 4;
+    cudaStream_t s = m->ctx->stream;
+    LLMRS_CUDA_TRY(cudaMemcpy2DAsync(h_k, row, m->layers[layer].kc, pitch, row, m->Hkv, cudaMemcpyDeviceToHost, s));
+    LLMRS_CUDA_TRY(cudaMemcpy2DAsync(h_v, row, m->layers[layer].vc, pitch, row, m->Hkv, cudaMemcpyDeviceToHost, s));
+    return finish_sync(m);
+}
+
+int llmrs_kv_fill_synthetic(llmrs_model *m, uint64_t seed, int n_pos)
+{
+    LLMRS_CHECK_ARG(m, "model is NULL");
+    LLMRS_CHECK_ARG(n_pos >= 0 && n_pos <= m->S, "n_pos %d exceeds max_seq %d", n_pos, m->S);
+    if (n_pos == 0)
+        return LLMRS_OK;
+    cudaSetDevice(m->ctx->device);
+    for (int l = 0; l < m->cfg.n_layers; l++)
+        LLMRS_TRY(synth_kv(m->ctx->stream, seed, l, 0, m->Hkv, n_pos, m->S, m->D, m->layers[l].kc, m->layers[l].vc));
+    return finish_sync(m);
+}
+
+// One decode step (src/core/model.rs:17-49 for a 1-token chunk).  The first
+// kernel launches without programmatic overlap, so the step's position and
+// token are settled before any kernel of the step runs; every later kernel
+// overlaps its weight prefetch with its predecessor.
+struct KernelTimer {
+    std::vector<cudaEvent_t> ev;
+    std::vector<int> kind;
+    int cap = 0;
+    int mark(cudaStream_t s, int k)
+    {
+        if ((int)kind.size() >= cap)
+            return LLMRS_OK;
+        cudaEvent_t e;
+        LLMRS_CUDA_TRY(cudaEventCreate(&e));
+        LLMRS_CUDA_TRY(cudaEventRecord(e, s));
+        ev.push_back(e);
+        kind.push_back(k);
+        return LLMRS_OK;
+    }
+};
+
+static int enqueue_step(llmrs_model *m, cudaStream_t s, KernelTimer *kt = nullptr)
+{
+    // with a timer every kernel is bracketed by events and launched without
+    // programmatic overlap, so each event pair times exactly one kernel
+    const bool overlap = kt == nullptr;
+    auto mark = [&](int kind) { return kt ? kt->mark(s, kind) : LLMRS_OK; };
+    const int H = m->H, F = m->F;
+    const int qkv_rows = (m->Hq + 2 * m->Hkv) * m->D;
+    const int sms = m->ctx->sms;
+    uint32_t *err = &m->state->err;
+    for (int l = 0; l < m->cfg.n_layers; l++) {
+        LayerW &L = m->layers[l];
+        GemvParams p{};
+        p.err = err;
+        p.eps = m->cfg.rms_eps;
+        // (1) input RMSNorm + Q8_0 + fused QKV projection (layer 0: embedding gather, src/main.rs:159-171)
+        p.w = L.qkv.w;
+        p.scales = L.qkv.s;
+        p.N = qkv_rows;
+        p.K = H;
+        p.x = m->x;
+        p.norm_w = L.attn_norm;
+        p.y = m->qkv;
+        p.state = m->state;
+        int pro = PRO_NORM;
+        if (l == 0) {
+            pro = PRO_EMBED_NORM;
+            p.embed = m->embed;
+            p.vocab = m->V;
+            p.x_out = m->x;
+        }
+        LLMRS_TRY(mark(0));
+        LLMRS_TRY(gemv_launch(p, m->wf, L.qkv.st, pro, EPI_STORE, s, overlap && l != 0, sms));
+        LLMRS_TRY(mark(-1));
+        // (2) RoPE + KV append + attention (src/core/layer.rs:175-333)
+        AttnParams a{};
+        a.qkv = m->qkv;
+        a.kc = L.kc;
+        a.vc = L.vc;
+        a.rope_cos = m->rope_cos;
+        a.rope_sin = m->rope_sin;
+        a.ctx = m->ctxv;
+        a.part = m->part;
+        a.counter = m->att_counter;
+        a.state = m->state;
+        a.err = err;
+        a.n_heads = m->Hq;
+        a.n_kv = m->Hkv;
+        a.head_dim = m->D;
+        a.max_seq = m->S;
+        a.n_splits = m->n_splits;
+        a.inv_sqrt_d = 1.0f / sqrtf((float)m->D);
+        LLMRS_TRY(mark(1));
+        LLMRS_TRY(attention_decode_launch(a, s, overlap));
+        LLMRS_TRY(mark(-1));
+        // (3) o_proj + residual (src/core/layer.rs:332, 386)
+        GemvParams o{};
+        o.err = err;
+        o.w = L.o.w;
+        o.scales = L.o.s;
+        o.N = H;
+        o.K = m->Hq * m->D;
+        o.x = m->ctxv;
+        o.y = m->x;
+        o.residual = m->x;
+        LLMRS_TRY(mark(2));
+        LLMRS_TRY(gemv_launch(o, m->wf, L.o.st, PRO_F32, EPI_RESIDUAL, s, overlap, sms));
+        LLMRS_TRY(mark(-1));
+        // (4) post RMSNorm + gate_up + SiLU*up (src/core/layer.rs:37-89)
+        GemvParams g{};
+        g.err = err;
+        g.eps = m->cfg.rms_eps;
+        g.w = L.gate_up.w;
+        g.scales = L.gate_up.s;
+        g.N = 2 * F;
+        g.K = H;
+        g.x = m->x;
+        g.norm_w = L.mlp_norm;
+        g.y = m->act;
+        LLMRS_TRY(mark(3));
+        LLMRS_TRY(gemv_launch(g, m->wf, L.gate_up.st, PRO_NORM, EPI_SILU, s, overlap, sms));
+        LLMRS_TRY(mark(-1));
+        // (5) down + residual (src/core/layer.rs:96, 403)
+        GemvParams d{};
+        d.err = err;
+        d.w = L.down.w;
+        d.scales = L.down.s;
+        d.N = H;
+        d.K = F;
+        d.x = m->act;
+        d.y = m->x;
+        d.residual = m->x;
+        LLMRS_TRY(mark(4));
+        LLMRS_TRY(gemv_launch(d, m->wf, L.down.st, PRO_F32, EPI_RESIDUAL, s, overlap, sms));
+        LLMRS_TRY(mark(-1));
+    }
+    // final RMSNorm + LM head + greedy argmax (src/core/model.rs:39-47, src/main.rs:185-190)
+    GemvParams h{};
+    h.err = err;
+    h.eps = m->cfg.rms_eps;
+    h.w = m->lm_head.w;
+    h.scales = m->lm_head.s;
+    h.N = m->V;
+    h.K = H;
+    h.x = m->x;
+    h.norm_w = m->final_norm;
+    h.y = m->logits;
+    h.state = m->state;
+    h.token_log = m->token_log;
+    LLMRS_TRY(mark(5));
+    LLMRS_TRY(gemv_launch(h, m->cfg.tied_embeddings ? 0 : m->wf, m->lm_head.st, PRO_NORM, EPI_ARGMAX, s,
+                          overlap, sms));
+    LLMRS_TRY(mark(-1));
+    return LLMRS_OK;
+}
+
+static int ensure_graph(llmrs_model *m)
+{
+    if (m->graph)
+        return LLMRS_OK;
+    cudaStream_t s = m->ctx->stream;
+    cudaGraph_t g = nullptr;
+    LLMRS_CUDA_TRY(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+    int rc = enqueue_step(m, s);
+    cudaError_t e = cudaStreamEndCapture(s, &g);
+    if (rc != LLMRS_OK) {
+        if (g)
+            cudaGraphDestroy(g);
+        return rc;
+    }
+    if (e != cudaSuccess)
+        return fail(LLMRS_ECUDA, "graph capture: %s", cudaGetErrorString(e));
+    e = cudaGraphInstantiate(&m->graph, g, 0);
+    cudaGraphDestroy(g);
+    if (e != cudaSuccess) {
+        m->graph = nullptr;
+        return fail(LLMRS_ECUDA, "graph instantiate: %s", cudaGetErrorString(e));
+    }
+    return LLMRS_OK;
+}
+
+static int check_state_err(llmrs_model *m, uint32_t e)
+{
+    if (!e)
+        return LLMRS_OK;
+    cudaMemsetAsync(&m->state->err, 0, 4, m->ctx->stream);
+    cudaStreamSynchronize(m->ctx->stream);
+    if (e == DEV_ERR_MBAR_TIMEOUT || e == DEV_ERR_PEER_TIMEOUT)
+        return fail(LLMRS_ETIMEDOUT, "decode step: device wait timed out (code %u)", e);
+    return fail(LLMRS_EDEVICE, "decode step: device error word %u (%s)", e,
+                e == DEV_ERR_BAD_TOKEN ? "token id out of range" : (e == DEV_ERR_BAD_POS ? "position out of range" : "?"));
+}
+
+// stage token/pos into the step state (8 bytes H2D from pinned memory)
+static int set_token_pos(llmrs_model *m, int token, int pos, int slot)
+{
+    int *hs = m->h_stage + 4 * slot;
+    hs[0] = token;
+    hs[1] = pos;
+    LLMRS_CUDA_TRY(cudaMemcpyAsync(m->state, hs, 2 * sizeof(int), cudaMemcpyHostToDevice, m->ctx->stream));
+    return LLMRS_OK;
+}
+
+int llmrs_decode_step(llmrs_model *m, int token, int pos, float *h_logits, int *h_argmax)
+{
+    LLMRS_CHECK_ARG(m, "model is NULL");
+    LLMRS_CHECK_ARG(token >= 0 && token < m->V, "token %d out of range [0,%d)", token, m->V);
+    LLMRS_CHECK_ARG(pos >= 0 && pos < m->S, "position %d out of range [0,%d)", pos, m->S);
+    cudaSetDevice(m->ctx->device);
+    LLMRS_TRY(ensure_graph(m));
+    cudaStream_t s = m->ctx->stream;
+    LLMRS_TRY(set_token_pos(m, token, pos, 0));
+    LLMRS_CUDA_TRY(cudaGraphLaunch(m->graph, s));
+    int *out = m->h_stage + 60;
+    LLMRS_CUDA_TRY(cudaMemcpyAsync(out, &m->state->token, sizeof(int), cudaMemcpyDeviceToHost, s));
+    LLMRS_CUDA_TRY(cudaMemcpyAsync(out + 1, &m->state->err, sizeof(int), cudaMemcpyDeviceToHost, s));
+    if (h_logits)
+        LLMRS_CUDA_TRY(cudaMemcpyAsync(h_logits, m->logits, (size_t)m->V * 4, cudaMemcpyDeviceToHost, s));
+    LLMRS_CUDA_TRY(cudaStreamSynchronize(s));
+    LLMRS_TRY(check_state_err(m, (uint32_t)out[1]));
+    if (h_argmax)
+        *h_argmax = out[0];
+    return LLMRS_OK;
+}
+
+int llmrs_generate(llmrs_model *m, int token, int pos, int n_steps, int *h_tokens_out)
+{
+    LLMRS_CHECK_ARG(m && h_tokens_out, "NULL argument");
+    LLMRS_CHECK_ARG(n_steps >= 0 && n_steps <= m->log_cap, "n_steps %d out of range", n_steps);
+    LLMRS_CHECK_ARG(token >= 0 && token < m->V, "token %d out of range", token);
+    LLMRS_CHECK_ARG(pos >= 0 && pos + n_steps <= m->S, "positions [%d,%d) exceed max_seq %d", pos, pos + n_steps, m->S);
+    if (n_steps == 0)
+        return LLMRS_OK;
+    cudaSetDevice(m->ctx->device);
+    LLMRS_TRY(ensure_graph(m));
+    cudaStream_t s = m->ctx->stream;
+    LLMRS_TRY(set_token_pos(m, token, pos, 0));
+    LLMRS_CUDA_TRY(cudaMemsetAsync(&m->state->n_log, 0, sizeof(int), s));
+    for (int i = 0; i < n_steps; i++)
+        LLMRS_CUDA_TRY(cudaGraphLaunch(m->graph, s));
+    int *out = m->h_stage + 60;
+    LLMRS_CUDA_TRY(cudaMemcpyAsync(out + 1, &m->state->err, sizeof(int), cudaMemcpyDeviceToHost, s));
+    LLMRS_CUDA_TRY(cudaMemcpyAsync(h_tokens_out, m->token_log, (size_t)n_steps * 4, cudaMemcpyDeviceToHost, s));
+    LLMRS_CUDA_TRY(cudaStreamSynchronize(s));
+    return check_state_err(m, (uint32_t)out[1]);
+}
+
+int llmrs_prefill(llmrs_model *m, const int *h_ids, int n, int start_pos, float *h_logits, int *h_argmax)
+{
+    LLMRS_CHECK_ARG(m && h_ids, "NULL argument");
+    LLMRS_CHECK_ARG(n >= 1 && start_pos >= 0 && start_pos + n <= m->S, "prefill of %d tokens at %d exceeds max_seq %d",
+                    n, start_pos, m->S);
+    for (int i = 0; i < n; i++)
+        LLMRS_CHECK_ARG(h_ids[i] >= 0 && h_ids[i] < m->V, "token id %d at %d out of range", h_ids[i], i);
+    cudaSetDevice(m->ctx->device);
+    LLMRS_TRY(ensure_graph(m));
+    cudaStream_t s = m->ctx->stream;
+    // Rows of a prefill chunk are causal and row-independent in every
+    // contraction (src/backend/cpu.rs:90-110, src/core/layer.rs:260-269), so
+    // the chunk is run as n consecutive single-row steps over the same cache.
+    for (int i = 0; i < n; i++) {
+        if (i % 12 == 0 && i > 0)
+            LLMRS_CUDA_TRY(cudaStreamSynchronize(s)); // recycle the 12 pinned staging slots
+        LLMRS_TRY(set_token_pos(m, h_ids[i], start_pos + i, 1 + (i % 12)));
+        LLMRS_CUDA_TRY(cudaGraphLaunch(m->graph, s));
+    }
+    int *out = m->h_stage + 60;
+    LLMRS_CUDA_TRY(cudaMemcpyAsync(out, &m->state->token, sizeof(int), cudaMemcpyDeviceToHost, s));
+    LLMRS_CUDA_TRY(cudaMemcpyAsync(out + 1, &m->state->err, sizeof(int), cudaMemcpyDeviceToHost, s));
+    if (h_logits)
+        LLMRS_CUDA_TRY(cudaMemcpyAsync(h_logits, m->logits, (size_t)m->V * 4, cudaMemcpyDeviceToHost, s));
+    LLMRS_CUDA_TRY(cudaStreamSynchronize(s));
+    LLMRS_TRY(check_state_err(m, (uint32_t)out[1]));
+    if (h_argmax)
+        *h_argmax = out[0];
+    return LLMRS_OK;
+}
+
+int llmrs_model_logits(llmrs_model *m, float *h_logits)
+{
+    LLMRS_CHECK_ARG(m && h_logits, "NULL argument");
+    cudaSetDevice(m->ctx->device);
+    LLMRS_CUDA_TRY(cudaMemcpyAsync(h_logits, m->logits, (size_t)m->V * 4, cudaMemcpyDeviceToHost, m->ctx->stream));
+    return finish_sync(m);
+}
+
+int llmrs_model_decode_kernel_count(llmrs_model *m, int *count)
+{
+    LLMRS_CHECK_ARG(m && count, "NULL argument");
+    *count = m->kernels_per_step;
+    return LLMRS_OK;
+}
+
+int llmrs_model_profile_decode(llmrs_model *m, int token, int pos, float *ms_out, int *kind_out, int *n)
+{
+    LLMRS_CHECK_ARG(m && ms_out && kind_out && n && *n > 0, "bad arguments");
+    LLMRS_CHECK_ARG(token >= 0 && token < m->V && pos >= 0 && pos < m->S, "token/position out of range");
+    cudaSetDevice(m->ctx->device);
+    cudaStream_t s = m->ctx->stream;
+    KernelTimer kt;
+    kt.cap = 2 * (*n);
+    LLMRS_TRY(set_token_pos(m, token, pos, 0));
+    int rc = enqueue_step(m, s, &kt);
+    cudaError_t e = cudaStreamSynchronize(s);
+    int cnt = 0;
+    for (size_t i = 0; i + 1 < kt.ev.size(); i += 2) {
+        float ms = 0;
+        if (e == cudaSuccess)
+            e = cudaEventElapsedTime(&ms, kt.ev[i], kt.ev[i + 1]);
+        if (cnt < *n) {
+            ms_out[cnt] = ms;
+            kind_out[cnt] = kt.kind[i];
+            cnt++;
+        }
+    }
+    for (auto ev : kt.ev)
+        cudaEventDestroy(ev);
+    *n = cnt;
+    LLMRS_TRY(rc);
+    if (e != cudaSuccess)
+        return fail(LLMRS_ECUDA, "profile: %s", cudaGetErrorString(e));
+    uint32_t err = 0;
+    LLMRS_CUDA_TRY(cudaMemcpy(&err, &m->state->err, 4, cudaMemcpyDeviceToHost));
+    return check_state_err(m, err);
+}
+
+int llmrs_model_time_decode(llmrs_model *m, int token, int pos, int iters, float *ms_total)
+{
+    LLMRS_CHECK_ARG(m && ms_total && iters > 0, "bad arguments");
+    LLMRS_CHECK_ARG(token >= 0 && token < m->V && pos >= 0 && pos + iters <= m->S, "token/position out of range");
+    cudaSetDevice(m->ctx->device);
+    LLMRS_TRY(ensure_graph(m));
+    cudaStream_t s = m->ctx->stream;
+    cudaEvent_t e0, e1;
+    LLMRS_CUDA_TRY(cudaEventCreate(&e0));
+    LLMRS_CUDA_TRY(cudaEventCreate(&e1));
+    LLMRS_TRY(set_token_pos(m, token, pos, 0));
+    LLMRS_CUDA_TRY(cudaMemsetAsync(&m->state->n_log, 0, sizeof(int), s));
+    LLMRS_CUDA_TRY(cudaEventRecord(e0, s));
+    for (int i = 0; i < iters; i++)
+        LLMRS_CUDA_TRY(cudaGraphLaunch(m->graph, s));
+    LLMRS_CUDA_TRY(cudaEventRecord(e1, s));
+    LLMRS_CUDA_TRY(cudaEventSynchronize(e1));
+    float ms = 0;
+    LLMRS_CUDA_TRY(cudaEventElapsedTime(&ms, e0, e1));
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    *ms_total = ms;
+    int *out = m->h_stage + 60;
+    LLMRS_CUDA_TRY(cudaMemcpy(out + 1, &m->state->err, sizeof(int), cudaMemcpyDeviceToHost));
+    return check_state_err(m, (uint32_t)out[1]);
+}
+
+} // extern "C"
