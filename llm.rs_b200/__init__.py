@@ -15,6 +15,7 @@ The directory name contains a dot, so load it by path, e.g.::
 """
 import ctypes
 import os
+import weakref
 
 import numpy as np
 
@@ -162,9 +163,15 @@ class Context:
         check(lib().llmrs_ctx_create(device, ctypes.byref(h)))
         self.h = h
         self.device = device
+        self._children = weakref.WeakSet()  # models / tensors that must go first
+
+    def _adopt(self, obj):
+        self._children.add(obj)
 
     def close(self):
         if self.h:
+            for child in list(self._children):
+                child._release()
             lib().llmrs_ctx_destroy(self.h)
             self.h = None
 
@@ -189,6 +196,7 @@ class DeviceTensor:
         p = ctypes.c_void_p()
         check(lib().llmrs_malloc(ctx.h, max(self.nbytes, 16), ctypes.byref(p)))
         self.ptr = p
+        ctx._adopt(self)
 
     @classmethod
     def from_numpy(cls, ctx, a, dtype=None):
@@ -205,9 +213,11 @@ class DeviceTensor:
         return out
 
     def free(self):
-        if self.ptr:
+        if self.ptr and self.ctx.h:
             lib().llmrs_free(self.ctx.h, self.ptr)
-            self.ptr = None
+        self.ptr = None
+
+    _release = free
 
     def __del__(self):
         try:
@@ -346,11 +356,14 @@ class Model:
         h = ctypes.c_void_p()
         check(lib().llmrs_model_create(ctx.h, ctypes.byref(c), ctypes.byref(h)))
         self.h = h
+        ctx._adopt(self)
 
     def close(self):
-        if self.h:
+        if self.h and self.ctx.h:
             lib().llmrs_model_destroy(self.h)
-            self.h = None
+        self.h = None
+
+    _release = close
 
     def __del__(self):
         try:

@@ -319,21 +319,51 @@ __global__ void __launch_bounds__(ATHREADS) attn_decode_kernel(const AttnParams 
     if (!s_last)
         return;
     __threadfence();
-    // last CTA of this KV head: merge the splits in order
-    for (int e = ctid; e < NREP * D; e += CWARPS * 32) {
-        const int h = e / D, d = e % D;
-        const float *src = p.part + (size_t)(g * NREP + h) * p.n_splits * PS;
+    // Last CTA of this KV head: merge the splits in split order.  First every
+    // (head, split) max / sum is fetched in parallel and turned into weights
+    // in shared memory; then each output element sums its split partials with
+    // all loads in flight together.
+    float *wsplit = wacc; // reuse: [NREP][n_splits] weights, then [NREP] totals
+    float *ltot = wacc + NREP * p.n_splits;
+    for (int e = ctid; e < NREP * p.n_splits; e += CWARPS * 32) {
+        const int h = e / p.n_splits, s = e % p.n_splits;
+        const float *src = p.part + ((size_t)(g * NREP + h) * p.n_splits + s) * PS;
+        wsplit[e] = __ldcg(src + D);               // m_s
+        ltot[NREP + e] = __ldcg(src + D + 1);      // l_s
+    }
+    named_bar_sync(1, CWARPS * 32);
+    if (ctid < NREP) {
+        const int h = ctid;
         float M = -INFINITY;
         for (int s = 0; s < p.n_splits; s++)
-            M = fmaxf(M, __ldcg(src + (size_t)s * PS + D));
-        float a = 0.0f, l = 0.0f;
+            M = fmaxf(M, wsplit[h * p.n_splits + s]);
+        float l = 0.0f;
         for (int s = 0; s < p.n_splits; s++) {
-            const float ms = __ldcg(src + (size_t)s * PS + D);
+            const float ms = wsplit[h * p.n_splits + s];
             const float f = (ms == -INFINITY) ? 0.0f : expf(ms - M);
-            a += __ldcg(src + (size_t)s * PS + d) * f;
-            l += __ldcg(src + (size_t)s * PS + D + 1) * f;
+            l += ltot[NREP + h * p.n_splits + s] * f;
+            wsplit[h * p.n_splits + s] = f;
         }
-        p.ctx[(size_t)(g * NREP + h) * D + d] = a / l;
+        ltot[h] = l;
+    }
+    named_bar_sync(1, CWARPS * 32);
+    for (int e = ctid; e < NREP * D; e += CWARPS * 32) {
+        const int h = e / D, d = e % D;
+        const float *src = p.part + (size_t)(g * NREP + h) * p.n_splits * PS + d;
+        float a = 0.0f;
+        int s = 0;
+        for (; s + 8 <= p.n_splits; s += 8) {
+            float v[8];
+#pragma unroll
+            for (int u = 0; u < 8; u++)
+                v[u] = __ldcg(src + (size_t)(s + u) * PS);
+#pragma unroll
+            for (int u = 0; u < 8; u++)
+                a += v[u] * wsplit[h * p.n_splits + s + u];
+        }
+        for (; s < p.n_splits; s++)
+            a += __ldcg(src + (size_t)s * PS) * wsplit[h * p.n_splits + s];
+        p.ctx[(size_t)(g * NREP + h) * D + d] = a / ltot[h];
     }
     if (ctid == 0)
         p.counter[g] = 0u;

@@ -131,7 +131,7 @@ __device__ __forceinline__ uint64_t globaltimer_ns()
 // Wait for the given phase parity; gives up after ~limit_ns and records the
 // timeout in *err.  Returns false on timeout.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint32_t *err,
-                                          uint64_t limit_ns = 2000000000ull)
+                                          uint64_t limit_ns = 500000000ull)
 {
     if (mbar_try_wait(bar, parity))
         return true;

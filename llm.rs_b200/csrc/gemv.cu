@@ -9,122 +9,176 @@
 // The activation is quantised to Q8_0 in the kernel's prologue exactly as
 // CpuBackend::quantize_row_q8_0 does (src/backend/cpu.rs:724-743).
 //
-// Data movement: each CTA owns a balanced, contiguous range of rows.  A
-// producer warp streams 32-row x 32-block chunks of nibbles (or int8 codes)
-// and their block scales from HBM into a ring of shared-memory stages with 1-D
-// bulk TMA copies (cp.async.bulk, mbarrier complete_tx), so HBM reads are
-// whole contiguous row segments.  Eight consumer warps compute with dp4a: lane
-// l takes block l of the chunk for each of its rows, so a warp reads 512
-// contiguous smem bytes per row (conflict-free).  The per-block products are
-// transposed through a small smem buffer so one lane per row adds them in the
-// reference's sequential block order.
+// Work split.  Each CTA owns rows [i*rows_per_cta, (i+1)*rows_per_cta), cut
+// into tiles of box_rows (<= 32) rows; a tile is processed in chunks of 32
+// blocks (1024 weights).  One (tile, chunk) pair is one pipeline stage.
+//
+// Data movement.  A producer thread streams each stage with 2-D tensor-map
+// TMA copies straight from the reference's planar layout (row-major nibbles /
+// int8 codes and row-major block scales): four (Q4) or eight (Q8) boxes of
+// rows x 128 bytes with 128-byte swizzle, plus one box of scales.  The swizzle
+// lets lane r read row r's 16-byte block at (r*128 + (chunk ^ (r & 7)) * 16)
+// without bank conflicts.
+//
+// Compute.  Consumer warp w takes stages w, w+4, w+8, ...; lane r of the warp
+// owns row r of the tile and computes that row's 32 block products with dp4a
+// (activation blocks are broadcast reads).  The products are then added to the
+// row's running f32 sum in block order; the running sum is handed from stage
+// to stage through shared memory (an mbarrier chain), so the reference's
+// sequential order holds across chunks while four stages are computed at once.
 //
 // The producer does not depend on the previous kernel, so with programmatic
-// dependent launch it starts streaming weights while the previous kernel is
-// still running; consumers call griddepcontrol.wait before reading activations.
+// dependent launch it streams weights while the previous kernel still runs;
+// consumers call griddepcontrol.wait before touching activations.
+#include <cudaTypedefs.h>
 #include <cuda_fp16.h>
+
+#include <mutex>
 
 #include "common.cuh"
 #include "gemv.cuh"
+
+// Optional phase tracing (cycle counters around pipeline waits); compiled out
+// unless a tracing build defines LLMRS_GEMV_TRACE and provides the hooks.
+#ifndef LLMRS_GEMV_TRACE
+#define LLMRS_TRACE_BEGIN(slot)
+#define LLMRS_TRACE_END(slot)
+#define LLMRS_TRACE_FLUSH(role)
+#define LLMRS_TRACE_PROLOG
+#endif
 
 namespace llmrs {
 
 namespace {
 
-constexpr int CW = 8;   // consumer warps
-constexpr int TR = 32;  // rows per tile (4 per consumer warp)
-constexpr int CB = 32;  // blocks per chunk (1024 weights)
-constexpr int NTHREADS = (CW + 1) * 32;
-constexpr int TB_STRIDE = 36; // floats per row of the transpose buffer (16-byte aligned, conflict-free)
-constexpr size_t SMEM_BUDGET = 112 * 1024; // two CTAs per SM (current + PDL-prefetching next kernel)
+constexpr int NG = 4;                    // consumer warp groups (one pipeline stage each)
+constexpr int WPG = 4;                   // warps per group
+constexpr int RPW = 8;                   // tile rows per warp (WPG * RPW = 32)
+constexpr int NW = NG * WPG;             // consumer warps
+constexpr int NTHREADS = (NW + 1) * 32;  // + producer warp
+constexpr int TR = 32;                   // max rows per tile
+constexpr int CB = 32;                   // blocks per chunk (1024 weights), one per lane
+constexpr int TBS = 36;                  // transpose row stride (floats): 16-byte aligned, conflict-free
+constexpr size_t SMEM_BUDGET = 200 * 1024; // one CTA per SM (544 threads): use most of the SM's shared memory
+constexpr int MAX_STAGES = 8;
+constexpr int PRO_THREADS = NW * 32;
 
 __host__ __device__ constexpr int wbytes_per_block(int wf) { return wf == 0 ? 16 : 32; }
 __host__ __device__ constexpr int sbytes(int st) { return st == 0 ? 2 : 4; }
-__host__ __device__ constexpr size_t align16(size_t x) { return (x + 15) & ~size_t(15); }
+__host__ __device__ constexpr size_t align_up(size_t x, size_t a) { return (x + a - 1) & ~(a - 1); }
 
 struct SmemLayout {
-    size_t stage_bytes, act_off, acts_off, actc_off, tbuf_off, bar_off, red_off, total;
+    size_t stage_bytes, scale_off, act_off, acts_off, actc_off, tb_off, link_off, bar_off, red_off, total;
 };
 
+// offsets are relative to a 128-byte aligned base
 __host__ __device__ inline SmemLayout smem_layout(int wf, int st, int K, int stages)
 {
     SmemLayout L;
-    int nb = K / 32;
-    L.stage_bytes = (size_t)TR * CB * (wbytes_per_block(wf) + sbytes(st));
+    const int nb = K / 32;
+    L.scale_off = (size_t)TR * CB * wbytes_per_block(wf);
+    L.stage_bytes = align_up(L.scale_off + (size_t)TR * CB * sbytes(st), 128);
     L.act_off = L.stage_bytes * stages;
     L.acts_off = L.act_off + (size_t)nb * 32;
-    L.actc_off = align16(L.acts_off + (size_t)nb * 4);
-    L.tbuf_off = align16(L.actc_off + (size_t)nb * 4);
-    L.bar_off = align16(L.tbuf_off + (size_t)CW * 4 * TB_STRIDE * 4);
-    L.red_off = L.bar_off + (size_t)stages * 2 * 8;
-    L.total = align16(L.red_off + 16 * 4);
+    L.actc_off = align_up(L.acts_off + (size_t)nb * 4, 16);
+    L.tb_off = align_up(L.actc_off + (size_t)nb * 4, 16);
+    L.link_off = L.tb_off + (size_t)NW * RPW * TBS * 4;
+    L.bar_off = align_up(L.link_off + (size_t)NW * RPW * 4, 16);
+    L.red_off = L.bar_off + (size_t)(2 * stages + NW) * 8;
+    L.total = align_up(L.red_off + 16 * 4, 16) + 128; // + slack to align the base
     return L;
 }
 
-// byte k (0..3) of packed word j (0..7) comes from lane src_lane(j, k)
+// ------------------------------------------------------------- activation
+// Quantise one 32-value block held by one thread (bit-exact Q8_0) and pack it
+// for the weight format: Q4 order puts the even elements of every 8 in words
+// 0-3 and the odd ones in words 4-7 (matching low / high nibbles), Q8 keeps
+// the natural order.
 template <int WF>
-__device__ __forceinline__ int src_lane(int j, int k)
+__device__ __forceinline__ void quantize_pack(const float (&v)[32], uint32_t *dst_words, float *dst_s, int *dst_c)
 {
-    if (WF == 0) // Q4 order: words 0-3 = even elements of each 8, words 4-7 = odd
-        return j < 4 ? 8 * j + 2 * k : 8 * (j - 4) + 2 * k + 1;
-    return 4 * j + k; // natural order
-}
-
-// Quantise one 32-value block held one value per lane (bit-exact Q8_0) and store
-// its packed codes (32 bytes), scale and correction term to shared memory.
-template <int WF>
-__device__ __forceinline__ void quantize_block(float v, int lane, uint32_t *dst_words, float *dst_s, int *dst_c)
-{
-    float amax = warp_max(fabsf(v));
-    int q = 0;
-    float scale = 0.0f;
+    float amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 32; i++)
+        amax = fmaxf(amax, fabsf(v[i]));
+    float scale = 0.0f, inv = 0.0f;
     if (amax != 0.0f) {
         scale = __fdiv_rn(amax, 127.0f);
-        float inv = __fdiv_rn(1.0f, scale);
-        float r = roundf(__fmul_rn(v, inv));
-        r = fminf(fmaxf(r, -127.0f), 127.0f);
-        q = (r != r) ? 0 : (int)r;
+        inv = __fdiv_rn(1.0f, scale);
     }
-    uint32_t word = 0;
-    int j = lane & 7;
+    int q[32];
+    int sum = 0;
 #pragma unroll
-    for (int k = 0; k < 4; k++) {
-        uint32_t b = (uint32_t)__shfl_sync(0xffffffffu, q & 0xFF, src_lane<WF>(j, k));
-        word |= b << (8 * k);
+    for (int i = 0; i < 32; i++) {
+        float r = roundf(__fmul_rn(v[i], inv));
+        r = fminf(fmaxf(r, -127.0f), 127.0f);
+        q[i] = (amax == 0.0f || r != r) ? 0 : (int)r;
+        sum += q[i];
     }
-    if (lane < 8)
-        dst_words[lane] = word;
-    int sum = warp_sum_int(q);
-    if (lane == 0) {
-        *dst_s = scale;
-        *dst_c = WF == 0 ? -8 * sum : 0;
+    uint32_t w[8];
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        uint32_t x = 0;
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const int e = WF == 0 ? (j < 4 ? 8 * j + 2 * k : 8 * (j - 4) + 2 * k + 1) : 4 * j + k;
+            x |= (uint32_t)(q[e] & 0xFF) << (8 * k);
+        }
+        w[j] = x;
+    }
+    reinterpret_cast<uint4 *>(dst_words)[0] = make_uint4(w[0], w[1], w[2], w[3]);
+    reinterpret_cast<uint4 *>(dst_words)[1] = make_uint4(w[4], w[5], w[6], w[7]);
+    *dst_s = scale;
+    *dst_c = WF == 0 ? -8 * sum : 0;
+}
+
+__device__ __forceinline__ void load32(const float *src, float (&v)[32])
+{
+    const float4 *s4 = reinterpret_cast<const float4 *>(src);
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        const float4 f = s4[i];
+        v[4 * i] = f.x;
+        v[4 * i + 1] = f.y;
+        v[4 * i + 2] = f.z;
+        v[4 * i + 3] = f.w;
     }
 }
 
-// Fill the shared-memory activation (codes, scales, corrections) from the
-// selected source.  Runs on the CW consumer warps (named barrier 1).
+// Fill the shared-memory activation (codes, scales, corrections).  One thread
+// per 32-block; `nthr` threads with ids `tid` take part; `bar` is a named
+// barrier id covering exactly those threads.
 template <int WF, int PRO>
-__device__ void load_activation(const GemvParams &p, uint32_t *act, float *act_s, int *act_c, float *red,
-                                int ctid, int warp, int lane)
+__device__ void load_activation(const GemvParams &p, uint32_t *act, float *act_s, int *act_c, float *red, int tid,
+                                int nthr, int bar)
 {
     const int K = p.K, nb = K >> 5;
     if (PRO == PRO_Q8) {
-        for (int b = warp; b < nb; b += CW) {
-            int q = p.xq[(size_t)b * 32 + lane];
-            uint32_t word = 0;
-            int j = lane & 7;
+        for (int b = tid; b < nb; b += nthr) {
+            const uint4 c0 = reinterpret_cast<const uint4 *>(p.xq + (size_t)b * 32)[0];
+            const uint4 c1 = reinterpret_cast<const uint4 *>(p.xq + (size_t)b * 32)[1];
+            const uint32_t in[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+            int q[32], sum = 0;
 #pragma unroll
-            for (int k = 0; k < 4; k++) {
-                uint32_t v = (uint32_t)__shfl_sync(0xffffffffu, q & 0xFF, src_lane<WF>(j, k));
-                word |= v << (8 * k);
+            for (int i = 0; i < 32; i++) {
+                q[i] = (int)(int8_t)(in[i >> 2] >> (8 * (i & 3)));
+                sum += q[i];
             }
-            if (lane < 8)
-                act[b * 8 + lane] = word;
-            int sum = warp_sum_int(q);
-            if (lane == 0) {
-                act_s[b] = p.xs[b];
-                act_c[b] = WF == 0 ? -8 * sum : 0;
+            uint32_t w[8];
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                uint32_t x = 0;
+#pragma unroll
+                for (int k = 0; k < 4; k++) {
+                    const int e = WF == 0 ? (j < 4 ? 8 * j + 2 * k : 8 * (j - 4) + 2 * k + 1) : 4 * j + k;
+                    x |= (uint32_t)(q[e] & 0xFF) << (8 * k);
+                }
+                w[j] = x;
             }
+            reinterpret_cast<uint4 *>(act + (size_t)b * 8)[0] = make_uint4(w[0], w[1], w[2], w[3]);
+            reinterpret_cast<uint4 *>(act + (size_t)b * 8)[1] = make_uint4(w[4], w[5], w[6], w[7]);
+            act_s[b] = p.xs[b];
+            act_c[b] = WF == 0 ? -8 * sum : 0;
         }
         return;
     }
@@ -132,39 +186,52 @@ __device__ void load_activation(const GemvParams &p, uint32_t *act, float *act_s
     if (PRO == PRO_EMBED_NORM) {
         int tok = p.state->token;
         if (tok < 0 || tok >= p.vocab) {
-            if (ctid == 0)
+            if (tid == 0)
                 atomicCAS(p.err, 0u, (uint32_t)DEV_ERR_BAD_TOKEN);
             tok = 0;
         }
         x = p.embed + (size_t)tok * K;
         if (blockIdx.x == 0)
-            for (int i = ctid; i < K; i += CW * 32)
+            for (int i = tid; i < K; i += nthr)
                 p.x_out[i] = x[i];
     }
     float scale = 1.0f;
     if (PRO == PRO_NORM || PRO == PRO_EMBED_NORM) {
+        // sum of squares in a fixed order (per thread, then a fixed tree)
         float ss = 0.0f;
-        for (int i = ctid; i < K; i += CW * 32)
-            ss = __fadd_rn(ss, __fmul_rn(x[i], x[i]));
-        ss = warp_sum(ss);
-        if (lane == 0)
-            red[warp] = ss;
-        named_bar_sync(1, CW * 32);
-        float tot = red[0];
+        for (int b = tid; b < nb; b += nthr) {
+            float v[32];
+            load32(x + (size_t)b * 32, v);
 #pragma unroll
-        for (int w = 1; w < CW; w++)
+            for (int i = 0; i < 32; i++)
+                ss = __fadd_rn(ss, __fmul_rn(v[i], v[i]));
+        }
+        ss = warp_sum(ss);
+        const int warp = tid >> 5;
+        if ((tid & 31) == 0)
+            red[warp] = ss;
+        named_bar_sync(bar, nthr);
+        float tot = red[0];
+        for (int w = 1; w < nthr / 32; w++)
             tot = __fadd_rn(tot, red[w]);
-        float rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)K), p.eps));
+        const float rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)K), p.eps));
         scale = __fdiv_rn(1.0f, rms);
     }
-    for (int b = warp; b < nb; b += CW) {
-        float v = x[(size_t)b * 32 + lane];
-        if (PRO == PRO_NORM || PRO == PRO_EMBED_NORM)
-            v = __fmul_rn(__fmul_rn(v, scale), p.norm_w[(size_t)b * 32 + lane]);
-        quantize_block<WF>(v, lane, act + (size_t)b * 8, act_s + b, act_c + b);
+    for (int b = tid; b < nb; b += nthr) {
+        float v[32];
+        load32(x + (size_t)b * 32, v);
+        if (PRO == PRO_NORM || PRO == PRO_EMBED_NORM) {
+            float wn[32];
+            load32(p.norm_w + (size_t)b * 32, wn);
+#pragma unroll
+            for (int i = 0; i < 32; i++)
+                v[i] = __fmul_rn(__fmul_rn(v[i], scale), wn[i]);
+        }
+        quantize_pack<WF>(v, act + (size_t)b * 8, act_s + b, act_c + b);
     }
 }
 
+// ------------------------------------------------------------- block dots
 __device__ __forceinline__ int dot_block_q4(const uint4 wv, const uint4 ae, const uint4 ao, int acc)
 {
     const uint32_t m = 0x0F0F0F0Fu;
@@ -200,18 +267,23 @@ __device__ __forceinline__ float load_scale(const uint8_t *base, int idx)
     return reinterpret_cast<const float *>(base)[idx];
 }
 
-// local row (within a 32-row tile) of slot s (0..3) of consumer warp w:
-// row pairs are dealt round-robin so partial tiles stay balanced and the two
-// rows of a pair (gate/up) sit in adjacent lanes of one warp.
-__device__ __forceinline__ int slot_row(int w, int s) { return 2 * (w + CW * (s >> 1)) + (s & 1); }
-
-// Last CTA of an argmax GEMV publishes the step's greedy token and advances
-// the decode position; the state is then ready for the next step.
-__device__ void argmax_finalize(const GemvParams &p, unsigned long long key)
+// 2-D tensor-map TMA load of a box at (x, y) into shared memory
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar,
+                                            uint64_t policy)
 {
-    __shared__ unsigned long long s_key[CW];
-    __shared__ unsigned int s_ticket;
-    int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_addr(dst)),
+        "l"(map), "r"(x), "r"(y), "r"(smem_addr(bar)), "l"(policy)
+        : "memory");
+}
+
+// Publish the step's greedy token: CTA max -> global atomicMax; the last CTA
+// writes the token, logs it and advances the decode position.
+__device__ void argmax_finalize(const GemvParams &p, unsigned long long key, int tid, int nthr, int bar)
+{
+    __shared__ unsigned long long s_key[32];
+    const int warp = tid >> 5, lane = tid & 31;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
         unsigned long long other = __shfl_xor_sync(0xffffffffu, key, o);
@@ -219,20 +291,20 @@ __device__ void argmax_finalize(const GemvParams &p, unsigned long long key)
     }
     if (lane == 0)
         s_key[warp] = key;
-    named_bar_sync(1, CW * 32);
-    if (threadIdx.x == 0) {
+    named_bar_sync(bar, nthr);
+    if (tid == 0) {
         unsigned long long k = s_key[0];
-        for (int w = 1; w < CW; w++)
+        for (int w = 1; w < nthr / 32; w++)
             k = s_key[w] > k ? s_key[w] : k;
         atomicMax(&p.state->key, k);
         __threadfence();
-        s_ticket = atomicAdd(&p.state->done, 1u);
-        if (s_ticket == gridDim.x - 1) {
+        const unsigned int ticket = atomicAdd(&p.state->done, 1u);
+        if (ticket == gridDim.x - 1) {
             __threadfence();
-            unsigned long long best = atomicAdd(&p.state->key, 0ull);
-            int tok = (int)argmax_key_index(best);
+            const unsigned long long best = atomicAdd(&p.state->key, 0ull);
+            const int tok = (int)argmax_key_index(best);
             StepState *st = p.state;
-            int n = st->n_log;
+            const int n = st->n_log;
             if (p.token_log && n < st->log_cap)
                 p.token_log[n] = tok;
             st->n_log = n + 1;
@@ -246,176 +318,211 @@ __device__ void argmax_finalize(const GemvParams &p, unsigned long long key)
 }
 
 template <int WF, int ST, int PRO, int EPI>
-__global__ void __launch_bounds__(NTHREADS, 1) gemv_tma_kernel(const GemvParams p)
+__global__ void __launch_bounds__(NTHREADS, 1)
+    gemv_tma_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap ts, const GemvParams p)
 {
     constexpr int WB = wbytes_per_block(WF);
-    constexpr int W_ROW = CB * WB;
+    constexpr int W_ROW = CB * WB;       // bytes of one row of a chunk (512 / 1024)
     constexpr int S_ROW = CB * sbytes(ST);
-    extern __shared__ __align__(128) uint8_t smem[];
+    extern __shared__ __align__(128) uint8_t smem_raw[];
 
     griddep_launch_dependents();
+    LLMRS_TRACE_PROLOG
 
+    uint8_t *smem = smem_raw + ((128u - (smem_addr(smem_raw) & 127u)) & 127u);
     const int S = p.n_stages;
     const int K = p.K, nb = K >> 5;
     const int nchunks = (nb + CB - 1) / CB;
     const SmemLayout L = smem_layout(WF, ST, K, S);
-    uint8_t *stages = smem;
     uint32_t *act = reinterpret_cast<uint32_t *>(smem + L.act_off);
     float *act_s = reinterpret_cast<float *>(smem + L.acts_off);
     int *act_c = reinterpret_cast<int *>(smem + L.actc_off);
-    float *tbuf = reinterpret_cast<float *>(smem + L.tbuf_off);
+    float *tbuf = reinterpret_cast<float *>(smem + L.tb_off);
+    float *linkbuf = reinterpret_cast<float *>(smem + L.link_off);
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + L.bar_off);
     uint64_t *empty = full + S;
+    uint64_t *link = empty + S; // link[w]: warp w hands its rows' running sums to the next group
     float *red = reinterpret_cast<float *>(smem + L.red_off);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    // balanced contiguous row range in units of row pairs
-    const int n_units = p.N >> 1;
-    const int u0 = (int)(((long long)blockIdx.x * n_units) / gridDim.x);
-    const int u1 = (int)(((long long)(blockIdx.x + 1) * n_units) / gridDim.x);
-    const int r0 = 2 * u0, r1 = 2 * u1;
-    const int ntiles = (r1 - r0 + TR - 1) / TR;
+    // A stage is owned by one warp group at a time; with more active groups
+    // than stages minus one, a parity wait on a stage barrier could alias a phase.
+    const int nga = max(1, min(NG, S - 1));
+    const int B = p.box_rows;
+    const int r0 = blockIdx.x * p.rows_per_cta;
+    const int r1 = min(p.N, r0 + p.rows_per_cta);
+    const int ntiles = (r1 - r0 + B - 1) / B;
     const int iters = ntiles * nchunks;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; s++) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], CW);
+            mbar_init(&empty[s], WPG); // released by the group's warps
         }
+        for (int w = 0; w < NW; w++)
+            mbar_init(&link[w], 1);
         fence_mbar_init();
     }
     __syncthreads();
 
-    if (warp == CW) {
+    if (warp == NW) {
         // ------------------------------------------------------------ producer
-        const uint64_t pol = policy_evict_first();
-        const size_t w_row_bytes = (size_t)nb * WB;
-        const size_t s_row_bytes = (size_t)nb * sbytes(ST);
-        const uint8_t *wbase = p.w;
-        const uint8_t *sbase = reinterpret_cast<const uint8_t *>(p.scales);
-        for (int it = 0; it < iters; it++) {
-            const int s = it % S;
-            if (it >= S && !mbar_wait(&empty[s], ((it / S) - 1) & 1, p.err))
-                return;
-            const int tile = it / nchunks, c = it % nchunks;
-            const int trow0 = r0 + tile * TR;
-            const int rows = min(TR, r1 - trow0);
-            const int nbc = min(CB, nb - c * CB);
-            if (lane == 0)
-                mbar_arrive_expect_tx(&full[s], (uint32_t)(rows * nbc * (WB + sbytes(ST))));
-            __syncwarp();
-            if (lane < rows) {
-                const int row = trow0 + lane;
-                uint8_t *st = stages + (size_t)s * L.stage_bytes;
-                bulk_g2s(st + (size_t)lane * W_ROW, wbase + (size_t)row * w_row_bytes + (size_t)c * W_ROW,
-                         (uint32_t)(nbc * WB), &full[s], pol);
-                bulk_g2s(st + (size_t)TR * W_ROW + (size_t)lane * S_ROW,
-                         sbase + (size_t)row * s_row_bytes + (size_t)c * S_ROW, (uint32_t)(nbc * sbytes(ST)),
-                         &full[s], pol);
+        // weights do not depend on the previous kernel: stream them right away
+        if (lane == 0) {
+            const uint64_t pol = policy_evict_first();
+            const uint32_t stage_tx = (uint32_t)(B * (W_ROW + S_ROW)); // whole boxes (OOB is zero-filled)
+            for (int it = 0; it < iters; it++) {
+                const int s = it % S;
+                LLMRS_TRACE_BEGIN(0);
+                if (it >= S && !mbar_wait(&empty[s], ((it / S) - 1) & 1, p.err))
+                    return;
+                LLMRS_TRACE_END(0);
+                const int tile = it / nchunks, c = it % nchunks;
+                const int y = r0 + tile * B;
+                uint8_t *st = smem + (size_t)s * L.stage_bytes;
+                mbar_arrive_expect_tx(&full[s], stage_tx);
+                tma_load_2d(st, &tw, c * (W_ROW / 4), y, &full[s], pol);
+                tma_load_2d(st + L.scale_off, &ts, c * CB, y, &full[s], pol);
             }
+            LLMRS_TRACE_FLUSH(1);
         }
         return;
     }
 
     // -------------------------------------------------------------- consumers
+    LLMRS_TRACE_BEGIN(1);
     griddep_wait();
+    LLMRS_TRACE_END(1);
+    LLMRS_TRACE_BEGIN(2);
     const int ctid = threadIdx.x;
-    load_activation<WF, PRO>(p, act, act_s, act_c, red, ctid, warp, lane);
-    named_bar_sync(1, CW * 32);
+    load_activation<WF, PRO>(p, act, act_s, act_c, red, ctid, PRO_THREADS, 1);
+    named_bar_sync(1, PRO_THREADS);
+    LLMRS_TRACE_END(2);
 
-    float *tb = tbuf + (size_t)warp * 4 * TB_STRIDE;
+    // warp (grp, wq): group grp = warp / WPG takes stages it = grp, grp+nga, ...;
+    // wq = warp % WPG takes tile rows wq*RPW .. +RPW-1.  Lane l = block l of the chunk.
+    const int grp = warp / WPG, wq = warp % WPG;
+    const int prevw = ((grp + nga - 1) % nga) * WPG + wq;
+    float *tb = tbuf + (size_t)warp * RPW * TBS;
+    // transposed roles: lane j sums row ri = j % RPW over blocks seg*8 .. seg*8+7
+    const int ri = lane % RPW, seg = lane / RPW;
     unsigned long long best = 0ull;
     bool ok = true;
-    for (int tile = 0; tile < ntiles; tile++) {
-        const int trow0 = r0 + tile * TR;
-        const int rows = min(TR, r1 - trow0);
-        float acc = 0.0f; // lane s < 4 owns the row of slot s
-        for (int c = 0; c < nchunks; c++) {
-            const int it = tile * nchunks + c;
-            const int s = it % S;
-            // after a timeout the warp keeps its control flow (results are
-            // discarded by the host, which sees the error word) but stops waiting
-            if (ok && !mbar_wait(&full[s], (it / S) & 1, p.err))
-                ok = false;
-            const uint8_t *st = stages + (size_t)s * L.stage_bytes;
-            const uint8_t *ssc = st + (size_t)TR * W_ROW;
-            const int nbc = min(CB, nb - c * CB);
-            const int b = c * CB + lane;
-            float t[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-            if (lane < nbc) {
-                const uint4 a0 = reinterpret_cast<const uint4 *>(act)[2 * b];
-                const uint4 a1 = reinterpret_cast<const uint4 *>(act)[2 * b + 1];
-                const float sa = act_s[b];
-                const int cz = act_c[b];
+    for (int it = grp; grp < nga && it < iters; it += nga) {
+        const int s = it % S;
+        const int tile = it / nchunks, c = it % nchunks;
+        const int trow0 = r0 + tile * B;
+        const int rows = min(B, r1 - trow0);
+        const int nbc = min(CB, nb - c * CB);
+        LLMRS_TRACE_BEGIN(3);
+        if (ok && !mbar_wait(&full[s], (it / S) & 1, p.err))
+            ok = false;
+        LLMRS_TRACE_END(3);
+        LLMRS_TRACE_BEGIN(4);
+        const uint8_t *st = smem + (size_t)s * L.stage_bytes;
+        float t[RPW];
+        {
+            const int b = c * CB + min(lane, nbc - 1);
+            const uint4 a0 = reinterpret_cast<const uint4 *>(act)[2 * b];
+            const uint4 a1 = reinterpret_cast<const uint4 *>(act)[2 * b + 1];
+            const float sa = act_s[b];
+            const int cz = act_c[b];
 #pragma unroll
-                for (int sl = 0; sl < 4; sl++) {
-                    const int lr = slot_row(warp, sl);
-                    if (lr < rows) {
-                        int isum;
-                        if (WF == 0) {
-                            const uint4 wv = *reinterpret_cast<const uint4 *>(st + (size_t)lr * W_ROW + lane * 16);
-                            isum = dot_block_q4(wv, a0, a1, cz);
-                        } else {
-                            const uint4 *wp = reinterpret_cast<const uint4 *>(st + (size_t)lr * W_ROW + lane * 32);
-                            isum = dot_block_q8(wp[0], wp[1], a0, a1, cz);
-                        }
-                        const float sw = load_scale<ST>(ssc + (size_t)lr * S_ROW, lane);
-                        t[sl] = __fmul_rn((float)isum, __fmul_rn(sw, sa));
-                    }
+            for (int i = 0; i < RPW; i++) {
+                const int lr = wq * RPW + i;
+                const uint8_t *wrow = st + (size_t)lr * W_ROW;
+                int isum;
+                if (WF == 0) {
+                    const uint4 wv = *reinterpret_cast<const uint4 *>(wrow + lane * 16);
+                    isum = dot_block_q4(wv, a0, a1, cz);
+                } else {
+                    const uint4 *wp = reinterpret_cast<const uint4 *>(wrow + lane * 32);
+                    isum = dot_block_q8(wp[0], wp[1], a0, a1, cz);
                 }
+                const float sw = load_scale<ST>(st + L.scale_off + (size_t)lr * S_ROW, lane);
+                t[i] = __fmul_rn((float)isum, __fmul_rn(sw, sa));
             }
-#pragma unroll
-            for (int sl = 0; sl < 4; sl++)
-                tb[sl * TB_STRIDE + lane] = t[sl];
-            __syncwarp();
-            if (lane < 4 && slot_row(warp, lane) < rows) {
-                const float *src = tb + lane * TB_STRIDE;
-                for (int j = 0; j < nbc; j += 4) {
-                    const float4 v = *reinterpret_cast<const float4 *>(src + j);
-                    acc = __fadd_rn(acc, v.x);
-                    acc = __fadd_rn(acc, v.y);
-                    acc = __fadd_rn(acc, v.z);
-                    acc = __fadd_rn(acc, v.w);
-                }
-            }
-            __syncwarp();
-            if (lane == 0)
-                mbar_arrive(&empty[s]);
         }
-        // ---- epilogue for this tile
-        const int lr = slot_row(warp, lane & 3);
-        const bool valid = lane < 4 && lr < rows;
-        const int row = trow0 + lr;
-        if (EPI == EPI_STORE) {
-            if (valid)
-                p.y[row] = acc;
-        } else if (EPI == EPI_RESIDUAL) {
-            if (valid)
-                p.y[row] = __fadd_rn(acc, p.residual[row]);
-        } else if (EPI == EPI_SILU) {
-            const float up = __shfl_down_sync(0xffffffffu, acc, 1);
-            if (valid && (lane & 1) == 0) {
-                const float g = acc;
-                const float silu = __fdiv_rn(g, __fadd_rn(1.0f, expf(-g)));
-                p.y[row >> 1] = __fmul_rn(silu, up);
+        // products are in registers: hand the stage back to the producer
+        __syncwarp();
+        if (lane == 0)
+            mbar_arrive(&empty[s]);
+        // transpose: lane j then holds row ri's products for blocks seg*8 .. +7
+#pragma unroll
+        for (int i = 0; i < RPW; i++)
+            tb[i * TBS + lane] = t[i];
+        __syncwarp();
+        const float4 v0 = *reinterpret_cast<const float4 *>(tb + ri * TBS + seg * 8);
+        const float4 v1 = *reinterpret_cast<const float4 *>(tb + ri * TBS + seg * 8 + 4);
+        const float v[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+        // running sum of row ri from the previous stage (same rows, previous group)
+        float acc = 0.0f;
+        if (it > 0) {
+            if (ok && !mbar_wait(&link[prevw], ((it - 1) / nga) & 1, p.err))
+                ok = false;
+            if (c > 0 && seg == 0)
+                acc = linkbuf[prevw * RPW + ri];
+        }
+        // add the chunk's blocks in order: segment 0 first, then 1, 2, 3
+        const bool live_row = wq * RPW + ri < rows;
+#pragma unroll
+        for (int sg = 0; sg < 4; sg++) {
+            if (sg > 0) {
+                const float prev = __shfl_up_sync(0xffffffffu, acc, RPW);
+                if (seg == sg)
+                    acc = prev;
             }
-        } else if (EPI == EPI_ARGMAX) {
-            if (valid) {
-                if (p.y)
+            if (seg == sg && live_row) {
+#pragma unroll
+                for (int k = 0; k < 8; k++)
+                    if (sg * 8 + k < nbc)
+                        acc = __fadd_rn(acc, v[k]);
+            }
+        }
+        __syncwarp();
+        if (seg == 3)
+            linkbuf[warp * RPW + ri] = acc;
+        __syncwarp();
+        if (lane == 0)
+            mbar_arrive(&link[warp]);
+        LLMRS_TRACE_END(4);
+        if (c == nchunks - 1) {
+            // ---- epilogue: lanes of segment 3 hold the complete rows
+            const int row = trow0 + wq * RPW + ri;
+            const bool valid = seg == 3 && live_row;
+            if (EPI == EPI_STORE) {
+                if (valid)
                     p.y[row] = acc;
-                const unsigned long long k = argmax_key(acc, (uint32_t)row);
-                best = k > best ? k : best;
+            } else if (EPI == EPI_RESIDUAL) {
+                if (valid)
+                    p.y[row] = __fadd_rn(acc, p.residual[row]);
+            } else if (EPI == EPI_SILU) {
+                const float up = __shfl_down_sync(0xffffffffu, acc, 1);
+                if (valid && (row & 1) == 0) {
+                    const float silu = __fdiv_rn(acc, __fadd_rn(1.0f, expf(-acc)));
+                    p.y[row >> 1] = __fmul_rn(silu, up);
+                }
+            } else if (EPI == EPI_ARGMAX) {
+                if (valid) {
+                    if (p.y)
+                        p.y[row] = acc;
+                    const unsigned long long k = argmax_key(acc, (uint32_t)row);
+                    best = k > best ? k : best;
+                }
             }
         }
     }
     if (EPI == EPI_ARGMAX)
-        argmax_finalize(p, best);
+        argmax_finalize(p, best, ctid, PRO_THREADS, 1);
+    LLMRS_TRACE_FLUSH(0);
 }
 
 // ------------------------------------------------------------------ fallback
 // One thread per output row, same arithmetic; activation quantised into smem.
+constexpr int SIMPLE_THREADS = 256;
+
 template <int WF, int ST, int PRO, int EPI>
-__global__ void __launch_bounds__(256) gemv_simple_kernel(const GemvParams p)
+__global__ void __launch_bounds__(SIMPLE_THREADS) gemv_simple_kernel(const GemvParams p)
 {
     extern __shared__ __align__(16) uint8_t smem[];
     griddep_launch_dependents();
@@ -424,11 +531,9 @@ __global__ void __launch_bounds__(256) gemv_simple_kernel(const GemvParams p)
     float *act_s = reinterpret_cast<float *>(smem + (size_t)nb * 32);
     int *act_c = reinterpret_cast<int *>(act_s + nb);
     float *red = reinterpret_cast<float *>(act_c + nb);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     griddep_wait();
-    // the prologue helper assumes CW warps; run it on warps 0..CW-1 (256 threads)
-    load_activation<WF, PRO>(p, act, act_s, act_c, red, threadIdx.x, warp, lane);
-    named_bar_sync(1, CW * 32);
+    load_activation<WF, PRO>(p, act, act_s, act_c, red, threadIdx.x, SIMPLE_THREADS, 1);
+    named_bar_sync(1, SIMPLE_THREADS);
     const int row = blockIdx.x * blockDim.x + threadIdx.x;
     unsigned long long best = 0ull;
     float row_acc = 0.0f;
@@ -474,7 +579,7 @@ __global__ void __launch_bounds__(256) gemv_simple_kernel(const GemvParams p)
     }
     if (EPI == EPI_SILU) {
         // rows (2i, 2i+1) are threads (2i, 2i+1) of this block
-        __shared__ float rows_acc[256];
+        __shared__ float rows_acc[SIMPLE_THREADS];
         rows_acc[threadIdx.x] = row_acc;
         __syncthreads();
         if (row < p.N && (row & 1) == 0 && row + 1 < p.N) {
@@ -484,7 +589,7 @@ __global__ void __launch_bounds__(256) gemv_simple_kernel(const GemvParams p)
         }
     }
     if (EPI == EPI_ARGMAX)
-        argmax_finalize(p, best);
+        argmax_finalize(p, best, threadIdx.x, SIMPLE_THREADS, 1);
 }
 
 constexpr int SIMPLE_SMEM_MAX = 200 * 1024;
@@ -493,7 +598,7 @@ template <int WF, int ST, int PRO, int EPI>
 cudaError_t prepare_one()
 {
     cudaError_t e = cudaFuncSetAttribute(gemv_tma_kernel<WF, ST, PRO, EPI>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BUDGET + 4096);
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BUDGET + 2048);
     if (e == cudaSuccess)
         e = cudaFuncSetAttribute(gemv_simple_kernel<WF, ST, PRO, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  SIMPLE_SMEM_MAX);
@@ -501,31 +606,65 @@ cudaError_t prepare_one()
 }
 
 template <int WF, int ST, int PRO, int EPI>
-int launch_one(const GemvParams &p0, bool fast, cudaStream_t stream, bool pdl, int max_ctas)
+int launch_one(const GemvPlan &plan, const GemvParams &p0, cudaStream_t stream, bool pdl)
 {
     GemvParams p = p0;
-    if (fast) {
-        int stages = 0;
-        size_t smem = gemv_smem_bytes(WF, ST, p.K, &stages);
-        p.n_stages = stages;
-        int grid = min(max_ctas, p.N / 2);
-        LLMRS_CUDA_TRY(launch(gemv_tma_kernel<WF, ST, PRO, EPI>, dim3(grid), dim3(NTHREADS), smem, stream, pdl, p));
+    if (plan.fast) {
+        p.n_stages = plan.stages;
+        p.box_rows = plan.box_rows;
+        p.rows_per_cta = plan.rows_per_cta;
+        LLMRS_CUDA_TRY(launch(gemv_tma_kernel<WF, ST, PRO, EPI>, dim3(plan.grid), dim3(NTHREADS), plan.smem, stream,
+                              pdl, plan.tw, plan.ts, p));
     } else {
         const int nb = p.K / 32;
         size_t smem = (size_t)nb * 40 + 64;
         LLMRS_CHECK_ARG(smem <= (size_t)SIMPLE_SMEM_MAX, "gemv: K=%d too large", p.K);
-        int grid = (p.N + 255) / 256;
-        LLMRS_CUDA_TRY(launch(gemv_simple_kernel<WF, ST, PRO, EPI>, dim3(grid), dim3(256), smem, stream, pdl, p));
+        int grid = (p.N + SIMPLE_THREADS - 1) / SIMPLE_THREADS;
+        LLMRS_CUDA_TRY(
+            launch(gemv_simple_kernel<WF, ST, PRO, EPI>, dim3(grid), dim3(SIMPLE_THREADS), smem, stream, pdl, p));
     }
+    return LLMRS_OK;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn()
+{
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+    });
+    return fn;
+}
+
+// 2-D map over `rows` rows of `row_bytes` bytes viewed as `elem`-byte elements
+int encode_2d(CUtensorMap *map, const void *base, int elem, size_t row_bytes, int rows, int box_x, int box_y,
+              CUtensorMapSwizzle swizzle)
+{
+    auto fn = encode_fn();
+    if (!fn)
+        return fail(LLMRS_ECUDA, "cuTensorMapEncodeTiled unavailable");
+    const CUtensorMapDataType dt = elem == 2 ? CU_TENSOR_MAP_DATA_TYPE_UINT16 : CU_TENSOR_MAP_DATA_TYPE_UINT32;
+    cuuint64_t dims[2] = {(cuuint64_t)(row_bytes / elem), (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
+    cuuint32_t box[2] = {(cuuint32_t)box_x, (cuuint32_t)box_y};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(map, dt, 2, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return fail(LLMRS_ECUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
     return LLMRS_OK;
 }
 
 } // namespace
 
-size_t gemv_smem_bytes(int wf, int st, int K, int *stages)
+static size_t smem_bytes_for(int wf, int st, int K, int *stages)
 {
     int best = 0;
-    for (int s = 6; s >= 2; s--) {
+    for (int s = MAX_STAGES; s >= 2; s--) {
         if (smem_layout(wf, st, K, s).total <= SMEM_BUDGET) {
             best = s;
             break;
@@ -536,51 +675,65 @@ size_t gemv_smem_bytes(int wf, int st, int K, int *stages)
     return best ? smem_layout(wf, st, K, best).total : 0;
 }
 
-bool gemv_fast_ok(const GemvParams &p, int wf, int st)
+int gemv_plan(GemvPlan *plan, const void *w, const void *scales, int N, int K, int wf, int st, bool pairs, int sms)
 {
-    if (p.K % 256 != 0 || p.N % 2 != 0 || p.N < 2)
-        return false;
-    if ((reinterpret_cast<uintptr_t>(p.w) & 15) || (reinterpret_cast<uintptr_t>(p.scales) & 15))
-        return false;
-    return gemv_smem_bytes(wf, st, p.K, nullptr) != 0;
+    LLMRS_CHECK_ARG(plan && w && scales, "gemv_plan: NULL argument");
+    LLMRS_CHECK_ARG(K > 0 && K % 32 == 0, "gemv: K=%d must be a positive multiple of 32", K);
+    LLMRS_CHECK_ARG(N > 0, "gemv: N=%d must be positive", N);
+    LLMRS_CHECK_ARG(!pairs || N % 2 == 0, "gemv: paired rows need an even row count");
+    *plan = GemvPlan();
+    plan->wf = wf;
+    plan->st = st;
+    plan->N = N;
+    plan->K = K;
+    const bool aligned = !((uintptr_t)w & 15) && !((uintptr_t)scales & 15);
+    int stages = 0;
+    const size_t smem = smem_bytes_for(wf, st, K, &stages);
+    if (K % 256 != 0 || !aligned || smem == 0 || N < 2)
+        return LLMRS_OK; // simple kernel
+    // rows per CTA so that the grid covers the SMs once, in tiles of <= 32 rows
+    int rc = (N + sms - 1) / sms;
+    if (pairs)
+        rc += rc & 1;
+    const int ntiles = (rc + TR - 1) / TR;
+    int box = (rc + ntiles - 1) / ntiles;
+    if (pairs)
+        box += box & 1;
+    plan->box_rows = box;
+    plan->rows_per_cta = ntiles * box;
+    plan->grid = (N + plan->rows_per_cta - 1) / plan->rows_per_cta;
+    plan->stages = stages;
+    plan->smem = smem;
+    const size_t wrow = wf == 0 ? (size_t)K / 2 : (size_t)K;
+    // codes: boxes of box rows x 512 (Q4) / 1024 (Q8) bytes
+    LLMRS_TRY(encode_2d(&plan->tw, w, 4, wrow, N, CB * wbytes_per_block(wf) / 4, box, CU_TENSOR_MAP_SWIZZLE_NONE));
+    LLMRS_TRY(encode_2d(&plan->ts, scales, sbytes(st), (size_t)(K / 32) * sbytes(st), N, CB, box,
+                        CU_TENSOR_MAP_SWIZZLE_NONE));
+    plan->fast = 1;
+    return LLMRS_OK;
 }
 
 // every (weight format, scale dtype, prologue, epilogue) the op-level API and the decode step use
-#define LLMRS_GEMV_VARIANTS(X) \
-    X(0, 0, PRO_F32, EPI_STORE) \
-    X(0, 0, PRO_NORM, EPI_STORE) \
-    X(0, 0, PRO_EMBED_NORM, EPI_STORE) \
-    X(0, 0, PRO_F32, EPI_RESIDUAL) \
-    X(0, 0, PRO_NORM, EPI_SILU) \
-    X(0, 0, PRO_NORM, EPI_ARGMAX) \
-    X(0, 1, PRO_F32, EPI_STORE) \
-    X(0, 1, PRO_NORM, EPI_STORE) \
-    X(0, 1, PRO_EMBED_NORM, EPI_STORE) \
-    X(0, 1, PRO_F32, EPI_RESIDUAL) \
-    X(0, 1, PRO_NORM, EPI_SILU) \
-    X(0, 1, PRO_NORM, EPI_ARGMAX) \
-    X(1, 0, PRO_F32, EPI_STORE) \
-    X(1, 0, PRO_NORM, EPI_STORE) \
-    X(1, 0, PRO_EMBED_NORM, EPI_STORE) \
-    X(1, 0, PRO_F32, EPI_RESIDUAL) \
-    X(1, 0, PRO_NORM, EPI_SILU) \
-    X(1, 0, PRO_NORM, EPI_ARGMAX) \
-    X(1, 1, PRO_F32, EPI_STORE) \
-    X(1, 1, PRO_NORM, EPI_STORE) \
-    X(1, 1, PRO_EMBED_NORM, EPI_STORE) \
-    X(1, 1, PRO_F32, EPI_RESIDUAL) \
-    X(1, 1, PRO_NORM, EPI_SILU) \
-    X(1, 1, PRO_NORM, EPI_ARGMAX)
+#define LLMRS_GEMV_VARIANTS(X)                                                                             \
+    X(0, 0, PRO_F32, EPI_STORE) X(0, 0, PRO_NORM, EPI_STORE) X(0, 0, PRO_EMBED_NORM, EPI_STORE)            \
+    X(0, 0, PRO_F32, EPI_RESIDUAL) X(0, 0, PRO_NORM, EPI_SILU) X(0, 0, PRO_NORM, EPI_ARGMAX)               \
+    X(0, 1, PRO_F32, EPI_STORE) X(0, 1, PRO_NORM, EPI_STORE) X(0, 1, PRO_EMBED_NORM, EPI_STORE)            \
+    X(0, 1, PRO_F32, EPI_RESIDUAL) X(0, 1, PRO_NORM, EPI_SILU) X(0, 1, PRO_NORM, EPI_ARGMAX)               \
+    X(1, 0, PRO_F32, EPI_STORE) X(1, 0, PRO_NORM, EPI_STORE) X(1, 0, PRO_EMBED_NORM, EPI_STORE)            \
+    X(1, 0, PRO_F32, EPI_RESIDUAL) X(1, 0, PRO_NORM, EPI_SILU) X(1, 0, PRO_NORM, EPI_ARGMAX)               \
+    X(1, 1, PRO_F32, EPI_STORE) X(1, 1, PRO_NORM, EPI_STORE) X(1, 1, PRO_EMBED_NORM, EPI_STORE)            \
+    X(1, 1, PRO_F32, EPI_RESIDUAL) X(1, 1, PRO_NORM, EPI_SILU) X(1, 1, PRO_NORM, EPI_ARGMAX)               \
+    X(0, 0, PRO_Q8, EPI_RESIDUAL) X(0, 1, PRO_Q8, EPI_RESIDUAL) X(1, 0, PRO_Q8, EPI_RESIDUAL)             \
+    X(1, 1, PRO_Q8, EPI_RESIDUAL)
 
-int gemv_launch(const GemvParams &p, int wf, int st, int pro, int epi, cudaStream_t stream, bool pdl, int max_ctas)
+int gemv_launch(const GemvPlan &plan, const GemvParams &p, int pro, int epi, cudaStream_t stream, bool pdl)
 {
-    LLMRS_CHECK_ARG(p.K > 0 && p.K % 32 == 0, "gemv: K=%d must be a positive multiple of 32", p.K);
-    LLMRS_CHECK_ARG(p.N > 0, "gemv: N=%d must be positive", p.N);
+    LLMRS_CHECK_ARG(p.N == plan.N && p.K == plan.K, "gemv: params do not match the plan");
     LLMRS_CHECK_ARG(epi != EPI_SILU || p.N % 2 == 0, "gemv: SiLU epilogue needs an even row count");
-    const bool fast = gemv_fast_ok(p, wf, st);
+    const int wf = plan.wf, st = plan.st;
 #define LLMRS_GEMV_CASE(WF, ST, PRO, EPI)                                                                   \
     if (wf == WF && st == ST && pro == PRO && epi == EPI)                                                  \
-        return launch_one<WF, ST, PRO, EPI>(p, fast, stream, pdl, max_ctas);
+        return launch_one<WF, ST, PRO, EPI>(plan, p, stream, pdl);
     LLMRS_GEMV_VARIANTS(LLMRS_GEMV_CASE)
 #undef LLMRS_GEMV_CASE
     return fail(LLMRS_ENOTSUP, "gemv: unsupported variant wf=%d st=%d pro=%d epi=%d", wf, st, pro, epi);

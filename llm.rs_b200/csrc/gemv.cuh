@@ -1,6 +1,7 @@
 // gemv.cuh - batch-1 quantised matrix-vector product (decode hot path).
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -52,17 +53,29 @@ struct GemvParams {
     StepState *state;      // EPI_ARGMAX / PRO_EMBED_NORM
     int *token_log;        // EPI_ARGMAX: appended greedy tokens
     uint32_t *err;         // device error word
-    int n_stages;
+    int n_stages;          // set by gemv_launch from the plan
+    int box_rows;
+    int rows_per_cta;
 };
 
-// Launch the fast (TMA-pipelined) kernel when the shape allows it (K % 256 == 0,
-// N even, 16-byte aligned operands); otherwise a simple row-per-thread kernel
-// with identical arithmetic.  wf: 0 = Q4_0, 1 = Q8_0; st: 0 = f16 scales, 1 = f32.
-int gemv_launch(const GemvParams &p, int wf, int st, int pro, int epi, cudaStream_t stream, bool pdl,
-                int max_ctas);
-// bytes of dynamic shared memory the fast kernel uses for this shape (0 = fallback)
-size_t gemv_smem_bytes(int wf, int st, int K, int *stages);
-bool gemv_fast_ok(const GemvParams &p, int wf, int st);
+// Launch geometry + TMA descriptors of one weight matrix, built once per weight.
+// Each CTA owns rows [i*rows_per_cta, (i+1)*rows_per_cta) and streams them as
+// tiles of box_rows rows x 32 blocks with 2-D tensor-map copies.
+struct GemvPlan {
+    CUtensorMap tw;    // codes: [N rows][K/2 or K bytes] viewed as u32 elements
+    CUtensorMap ts;    // scales: [N rows][K/32] f16 or f32
+    int fast = 0;      // 0: shape needs the simple fallback kernel
+    int wf = 0, st = 0, N = 0, K = 0;
+    int box_rows = 0, rows_per_cta = 0, grid = 0, stages = 0;
+    size_t smem = 0;
+};
+
+// wf: 0 = Q4_0, 1 = Q8_0; st: 0 = f16 scales, 1 = f32.  pairs: row pairs must
+// stay in one tile (SiLU epilogue over interleaved gate/up rows).
+int gemv_plan(GemvPlan *plan, const void *w, const void *scales, int N, int K, int wf, int st, bool pairs,
+              int sms);
+// p.w / p.scales / p.N / p.K must match the plan
+int gemv_launch(const GemvPlan &plan, const GemvParams &p, int pro, int epi, cudaStream_t stream, bool pdl);
 // set kernel attributes (dynamic smem limits) for every variant on the current device;
 // called once per context, outside any stream capture
 int gemv_prepare(void);

@@ -70,6 +70,7 @@ struct QW {
     void *s = nullptr;    // scales
     int n = 0, k = 0;
     int st = 0;           // LLMRS_F16 / LLMRS_F32
+    GemvPlan plan;        // launch geometry + tensor maps (weights never move)
 };
 
 struct LayerW {
@@ -309,6 +310,9 @@ static int gemv_op(llmrs_ctx *ctx, int wf, const float *a, const void *w, const 
     LLMRS_CHECK_ARG(ctx && a && w && scales && c, "NULL argument");
     LLMRS_CHECK_ARG(m >= 1 && k >= 32 && k % 32 == 0 && n >= 1, "matmul_transposed: m=%d k=%d n=%d (k must be a multiple of 32)", m, k, n);
     LLMRS_CHECK_ARG(st == LLMRS_F16 || st == LLMRS_F32, "scale_dtype %d unknown", st);
+    LLMRS_CHECK_ARG(!((uintptr_t)a & 15), "matmul_transposed: activation pointer must be 16-byte aligned");
+    GemvPlan plan;
+    LLMRS_TRY(gemv_plan(&plan, w, scales, n, k, wf, st, false, ctx->sms));
     // rows of A are independent (the m>1 path quantises each row, src/backend/cpu.rs:90-110)
     for (int i = 0; i < m; i++) {
         GemvParams p{};
@@ -319,7 +323,7 @@ static int gemv_op(llmrs_ctx *ctx, int wf, const float *a, const void *w, const 
         p.x = a + (size_t)i * k;
         p.y = c + (size_t)i * n;
         p.err = ctx->d_err;
-        LLMRS_TRY(gemv_launch(p, wf, st, PRO_F32, EPI_STORE, ctx->stream, false, ctx->sms));
+        LLMRS_TRY(gemv_launch(plan, p, PRO_F32, EPI_STORE, ctx->stream, false));
     }
     return LLMRS_OK;
 }
@@ -528,6 +532,28 @@ int llmrs_model_create(llmrs_ctx *ctx, const llmrs_config *cfg, llmrs_model **ou
     if (!m->token_log) {
         model_free(m);
         return fail(LLMRS_ENOMEM, "model arena layout overflow");
+    }
+    {
+        const int sms = ctx->sms;
+        int rc = LLMRS_OK;
+        for (auto &L : m->layers) {
+            if (rc == LLMRS_OK)
+                rc = gemv_plan(&L.qkv.plan, L.qkv.w, L.qkv.s, L.qkv.n, L.qkv.k, wf, L.qkv.st, false, sms);
+            if (rc == LLMRS_OK)
+                rc = gemv_plan(&L.o.plan, L.o.w, L.o.s, L.o.n, L.o.k, wf, L.o.st, false, sms);
+            if (rc == LLMRS_OK)
+                rc = gemv_plan(&L.gate_up.plan, L.gate_up.w, L.gate_up.s, L.gate_up.n, L.gate_up.k, wf, L.gate_up.st,
+                               true, sms);
+            if (rc == LLMRS_OK)
+                rc = gemv_plan(&L.down.plan, L.down.w, L.down.s, L.down.n, L.down.k, wf, L.down.st, false, sms);
+        }
+        if (rc == LLMRS_OK)
+            rc = gemv_plan(&m->lm_head.plan, m->lm_head.w, m->lm_head.s, m->lm_head.n, m->lm_head.k,
+                           cfg->tied_embeddings ? 0 : wf, m->lm_head.st, false, sms);
+        if (rc != LLMRS_OK) {
+            model_free(m);
+            return rc;
+        }
     }
     cudaStream_t s = ctx->stream;
     e = cudaMemsetAsync(m->arena.base, 0, total, s);
@@ -762,7 +788,6 @@ static int enqueue_step(llmrs_model *m, cudaStream_t s, KernelTimer *kt = nullpt
     auto mark = [&](int kind) { return kt ? kt->mark(s, kind) : LLMRS_OK; };
     const int H = m->H, F = m->F;
     const int qkv_rows = (m->Hq + 2 * m->Hkv) * m->D;
-    const int sms = m->ctx->sms;
     uint32_t *err = &m->state->err;
     for (int l = 0; l < m->cfg.n_layers; l++) {
         LayerW &L = m->layers[l];
@@ -786,7 +811,7 @@ static int enqueue_step(llmrs_model *m, cudaStream_t s, KernelTimer *kt = nullpt
             p.x_out = m->x;
         }
         LLMRS_TRY(mark(0));
-        LLMRS_TRY(gemv_launch(p, m->wf, L.qkv.st, pro, EPI_STORE, s, overlap && l != 0, sms));
+        LLMRS_TRY(gemv_launch(L.qkv.plan, p, pro, EPI_STORE, s, overlap && l != 0));
         LLMRS_TRY(mark(-1));
         // (2) RoPE + KV append + attention (src/core/layer.rs:175-333)
         AttnParams a{};
@@ -820,7 +845,7 @@ static int enqueue_step(llmrs_model *m, cudaStream_t s, KernelTimer *kt = nullpt
         o.y = m->x;
         o.residual = m->x;
         LLMRS_TRY(mark(2));
-        LLMRS_TRY(gemv_launch(o, m->wf, L.o.st, PRO_F32, EPI_RESIDUAL, s, overlap, sms));
+        LLMRS_TRY(gemv_launch(L.o.plan, o, PRO_F32, EPI_RESIDUAL, s, overlap));
         LLMRS_TRY(mark(-1));
         // (4) post RMSNorm + gate_up + SiLU*up (src/core/layer.rs:37-89)
         GemvParams g{};
@@ -834,7 +859,7 @@ static int enqueue_step(llmrs_model *m, cudaStream_t s, KernelTimer *kt = nullpt
         g.norm_w = L.mlp_norm;
         g.y = m->act;
         LLMRS_TRY(mark(3));
-        LLMRS_TRY(gemv_launch(g, m->wf, L.gate_up.st, PRO_NORM, EPI_SILU, s, overlap, sms));
+        LLMRS_TRY(gemv_launch(L.gate_up.plan, g, PRO_NORM, EPI_SILU, s, overlap));
         LLMRS_TRY(mark(-1));
         // (5) down + residual (src/core/layer.rs:96, 403)
         GemvParams d{};
@@ -847,7 +872,7 @@ static int enqueue_step(llmrs_model *m, cudaStream_t s, KernelTimer *kt = nullpt
         d.y = m->x;
         d.residual = m->x;
         LLMRS_TRY(mark(4));
-        LLMRS_TRY(gemv_launch(d, m->wf, L.down.st, PRO_F32, EPI_RESIDUAL, s, overlap, sms));
+        LLMRS_TRY(gemv_launch(L.down.plan, d, PRO_F32, EPI_RESIDUAL, s, overlap));
         LLMRS_TRY(mark(-1));
     }
     // final RMSNorm + LM head + greedy argmax (src/core/model.rs:39-47, src/main.rs:185-190)
@@ -864,8 +889,7 @@ static int enqueue_step(llmrs_model *m, cudaStream_t s, KernelTimer *kt = nullpt
     h.state = m->state;
     h.token_log = m->token_log;
     LLMRS_TRY(mark(5));
-    LLMRS_TRY(gemv_launch(h, m->cfg.tied_embeddings ? 0 : m->wf, m->lm_head.st, PRO_NORM, EPI_ARGMAX, s,
-                          overlap, sms));
+    LLMRS_TRY(gemv_launch(m->lm_head.plan, h, PRO_NORM, EPI_ARGMAX, s, overlap));
     LLMRS_TRY(mark(-1));
     return LLMRS_OK;
 }

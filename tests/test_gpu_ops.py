@@ -84,7 +84,7 @@ def test_q4_small_and_ragged_shapes(llmrs, ctx, be, orc, rng, m, k, n):
     assert np.array_equal(bits(y), bits(ref))
     # and against the dequantised weights (only Q8 activation rounding differs)
     deq = orc.dequantize_q4(qs, sc, w.size).reshape(n, k).astype(np.float64)
-    assert np.abs(y - a.astype(np.float64) @ deq.T).max() < 0.05 * np.sqrt(k / 128)
+    assert np.abs(y - a.astype(np.float64) @ deq.T).max() < 0.1 * np.sqrt(k / 128)
 
 
 @pytest.mark.parametrize("n,k", [(4096, 4096), (1024, 14336), (256, 512)])
