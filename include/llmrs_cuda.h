@@ -119,6 +119,17 @@ int llmrs_scale(llmrs_ctx *ctx, const float *d_x, float *d_y, size_t n, float va
 /* Backend::copy_from (src/backend/cpu.rs:437-446) */
 int llmrs_copy_from(llmrs_ctx *ctx, const float *d_src, float *d_dst, size_t n);
 
+/* Fused decode attention for one token at position pos over a device KV cache
+ * (the per-head loop of src/core/layer.rs:175-333 for seq == 1, native GQA):
+ * RoPE(q), RoPE(k_new) with the caller's [max_seq][head_dim/2] cos/sin tables
+ * (llmrs_rope_table), append k_new / v_new at pos, softmax(q.k / sqrt(D)) over
+ * positions [0, pos], out = P.V.  d_qkv = q [n_heads*D] | k [n_kv*D] | v [n_kv*D];
+ * caches [n_kv][max_seq][D] f32 (position-major).  Split partials live in
+ * scratch memory owned by the context (allocated on first use). */
+int llmrs_attention_decode(llmrs_ctx *ctx, const float *d_qkv, float *d_kcache, float *d_vcache,
+                           const float *d_rope_cos, const float *d_rope_sin, float *d_out, int n_heads,
+                           int n_kv_heads, int head_dim, int max_seq, int pos);
+
 /* CpuBackend::quantize_row_q8_0 (src/backend/cpu.rs:663-745) for rows of k
  * values: codes [rows][k] and f32 scales [rows][k/32]; bit-exact */
 int llmrs_quantize_row_q8_0(llmrs_ctx *ctx, const float *d_x, int8_t *d_q, float *d_s, int rows, int k);

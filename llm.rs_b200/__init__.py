@@ -40,6 +40,7 @@ EXPORTS = [
     "llmrs_model_set_weight", "llmrs_kv_fill", "llmrs_kv_fill_synthetic", "llmrs_kv_read",
     "llmrs_decode_step", "llmrs_generate", "llmrs_prefill", "llmrs_model_logits", "llmrs_rope_table",
     "llmrs_model_decode_kernel_count", "llmrs_model_time_decode", "llmrs_model_profile_decode",
+    "llmrs_attention_decode",
 ]
 
 
@@ -120,6 +121,7 @@ def lib():
         "llmrs_model_decode_kernel_count": (ci, [vp, ip]),
         "llmrs_model_time_decode": (ci, [vp, ci, ci, ci, fp]),
         "llmrs_model_profile_decode": (ci, [vp, ci, ci, vp, vp, ip]),
+        "llmrs_attention_decode": (ci, [vp, vp, vp, vp, vp, vp, vp, ci, ci, ci, ci, ci]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -327,6 +329,14 @@ class CudaBackend:
         y = self._out(t.shape)
         check(lib().llmrs_copy_from(self.ctx.h, t.ptr, y.ptr, t.size))
         return y
+
+    def attention_decode(self, qkv, kcache, vcache, rope_cos, rope_sin, n_heads, n_kv_heads, head_dim, pos):
+        """Fused decode attention (one token at `pos`); appends k/v to the caches."""
+        out = self._out((n_heads * head_dim,))
+        max_seq = kcache.shape[1]
+        check(lib().llmrs_attention_decode(self.ctx.h, qkv.ptr, kcache.ptr, vcache.ptr, rope_cos.ptr, rope_sin.ptr,
+                                           out.ptr, n_heads, n_kv_heads, head_dim, max_seq, pos))
+        return out
 
     # CpuBackend::quantize_row_q8_0 and Tensor::quantize_q4 (bit-exact)
     def quantize_row_q8_0(self, x):

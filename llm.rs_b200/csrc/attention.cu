@@ -98,7 +98,7 @@ __global__ void __launch_bounds__(ATHREADS) attn_decode_kernel(const AttnParams 
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int split = blockIdx.x, g = blockIdx.y;
-    const int pos = p.state->pos;
+    const int pos = p.state ? p.state->pos : p.pos_fixed;
     const bool pos_ok = pos >= 0 && pos < p.max_seq;
     const int Lc = pos_ok ? pos : 0;           // cached positions [0, pos)
     const int t0 = (int)(((long long)split * Lc) / p.n_splits);

@@ -16,7 +16,8 @@ struct AttnParams {
     float *ctx;              // [Hq*D] attention output (context)
     float *part;             // split partials [Hq][n_splits][D + 2]
     unsigned int *counter;   // [Hkv] split completion tickets (left at 0)
-    const StepState *state;  // decode position
+    const StepState *state;  // decode position (nullptr: use pos_fixed)
+    int pos_fixed;
     uint32_t *err;
     int n_heads, n_kv, head_dim, max_seq, n_splits;
     float inv_sqrt_d;        // 1 / sqrt(D), as src/core/layer.rs:258 computes it

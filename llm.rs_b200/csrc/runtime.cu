@@ -61,6 +61,8 @@ struct llmrs_ctx {
     cudaStream_t own = nullptr;
     cudaStream_t stream = nullptr;
     uint32_t *d_err = nullptr; // op-level device error word
+    void *scratch = nullptr;   // op-level scratch (attention split partials), grown on demand
+    size_t scratch_bytes = 0;
 };
 
 namespace {
@@ -212,6 +214,8 @@ int llmrs_ctx_destroy(llmrs_ctx *ctx)
         return LLMRS_OK;
     cudaSetDevice(ctx->device);
     cudaStreamSynchronize(ctx->stream);
+    if (ctx->scratch)
+        cudaFree(ctx->scratch);
     if (ctx->d_err)
         cudaFree(ctx->d_err);
     if (ctx->own)
@@ -398,6 +402,55 @@ int llmrs_copy_from(llmrs_ctx *ctx, const float *d_src, float *d_dst, size_t n)
 {
     LLMRS_CHECK_ARG(ctx && (n == 0 || (d_src && d_dst)), "copy_from: bad arguments");
     return n ? op_copy(ctx->stream, d_src, d_dst, n) : LLMRS_OK;
+}
+
+static int ctx_scratch(llmrs_ctx *ctx, size_t bytes, void **out)
+{
+    if (ctx->scratch_bytes < bytes) {
+        LLMRS_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+        if (ctx->scratch)
+            cudaFree(ctx->scratch);
+        ctx->scratch = nullptr;
+        ctx->scratch_bytes = 0;
+        cudaError_t e = cudaMalloc(&ctx->scratch, bytes);
+        if (e != cudaSuccess)
+            return fail(LLMRS_ENOMEM, "scratch of %zu bytes: %s", bytes, cudaGetErrorString(e));
+        ctx->scratch_bytes = bytes;
+    }
+    *out = ctx->scratch;
+    return LLMRS_OK;
+}
+
+int llmrs_attention_decode(llmrs_ctx *ctx, const float *d_qkv, float *d_kcache, float *d_vcache,
+                           const float *d_rope_cos, const float *d_rope_sin, float *d_out, int n_heads,
+                           int n_kv_heads, int head_dim, int max_seq, int pos)
+{
+    LLMRS_CHECK_ARG(ctx && d_qkv && d_kcache && d_vcache && d_rope_cos && d_rope_sin && d_out, "NULL argument");
+    LLMRS_CHECK_ARG(n_kv_heads > 0 && n_heads > 0 && n_heads % n_kv_heads == 0, "bad head counts %d/%d", n_heads,
+                    n_kv_heads);
+    LLMRS_CHECK_ARG(max_seq > 0 && pos >= 0 && pos < max_seq, "position %d outside [0,%d)", pos, max_seq);
+    AttnParams a{};
+    a.n_heads = n_heads;
+    a.n_kv = n_kv_heads;
+    a.head_dim = head_dim;
+    a.max_seq = max_seq;
+    a.n_splits = attention_default_splits(n_kv_heads);
+    a.pos_fixed = pos;
+    a.qkv = d_qkv;
+    a.kc = d_kcache;
+    a.vc = d_vcache;
+    a.rope_cos = d_rope_cos;
+    a.rope_sin = d_rope_sin;
+    a.ctx = d_out;
+    a.err = ctx->d_err;
+    a.inv_sqrt_d = 1.0f / sqrtf((float)head_dim);
+    const size_t part = attention_partials_floats(n_heads, head_dim, a.n_splits) * 4;
+    void *scr = nullptr;
+    LLMRS_TRY(ctx_scratch(ctx, part + (size_t)n_kv_heads * 4 + 256, &scr));
+    a.part = reinterpret_cast<float *>(scr);
+    a.counter = reinterpret_cast<unsigned int *>(reinterpret_cast<uint8_t *>(scr) + ((part + 255) & ~size_t(255)));
+    LLMRS_CUDA_TRY(cudaMemsetAsync(a.counter, 0, (size_t)n_kv_heads * 4, ctx->stream));
+    return attention_decode_launch(a, ctx->stream, false);
 }
 
 int llmrs_quantize_row_q8_0(llmrs_ctx *ctx, const float *d_x, int8_t *d_q, float *d_s, int rows, int k)
