@@ -130,6 +130,25 @@ int llmrs_attention_decode(llmrs_ctx *ctx, const float *d_qkv, float *d_kcache, 
                            const float *d_rope_cos, const float *d_rope_sin, float *d_out, int n_heads,
                            int n_kv_heads, int head_dim, int max_seq, int pos);
 
+/* The same decode attention for callers that cannot allocate device memory
+ * (their memory belongs to another allocator that must account for every byte,
+ * or they must not allocate after start-up, or they cannot create an llmrs_ctx).
+ * No counterpart in the reference: it adds no op, only a way to call this one.
+ * Runs on the caller's cuda_stream (NULL = legacy default stream) on the current
+ * device; the caller passes every input and output.  Split partials and tickets
+ * use a fixed array linked into the library (2 MiB + 1 KiB, held by every GPU
+ * that loads the library until exit): n_heads * splits * (head_dim + 2) floats
+ * must fit in 2 MiB and n_kv_heads <= 128, else LLMRS_EINVAL.  Nothing is
+ * allocated: no cudaMalloc/cudaFree.  The first call on a device resolves the
+ * array's device address and sets kernel attributes; make that first call before
+ * any stream capture.  All calls share the one array: calls that overlap on the
+ * GPU (other streams, other host threads) race and must be serialised by the
+ * caller.  Bounded device waits that time out set *d_err (optional device word;
+ * NULL keeps the status inside the library, unreported). */
+int llmrs_attention_decode_noalloc(void *cuda_stream, const float *d_qkv, float *d_kcache, float *d_vcache,
+                                   const float *d_rope_cos, const float *d_rope_sin, float *d_out, int n_heads,
+                                   int n_kv_heads, int head_dim, int max_seq, int pos, unsigned int *d_err);
+
 /* CpuBackend::quantize_row_q8_0 (src/backend/cpu.rs:663-745) for rows of k
  * values: codes [rows][k] and f32 scales [rows][k/32]; bit-exact */
 int llmrs_quantize_row_q8_0(llmrs_ctx *ctx, const float *d_x, int8_t *d_q, float *d_s, int rows, int k);

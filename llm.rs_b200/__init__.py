@@ -40,7 +40,7 @@ EXPORTS = [
     "llmrs_model_set_weight", "llmrs_kv_fill", "llmrs_kv_fill_synthetic", "llmrs_kv_read",
     "llmrs_decode_step", "llmrs_generate", "llmrs_prefill", "llmrs_model_logits", "llmrs_rope_table",
     "llmrs_model_decode_kernel_count", "llmrs_model_time_decode", "llmrs_model_profile_decode",
-    "llmrs_attention_decode",
+    "llmrs_attention_decode", "llmrs_attention_decode_noalloc",
 ]
 
 
@@ -122,6 +122,7 @@ def lib():
         "llmrs_model_time_decode": (ci, [vp, ci, ci, ci, fp]),
         "llmrs_model_profile_decode": (ci, [vp, ci, ci, vp, vp, ip]),
         "llmrs_attention_decode": (ci, [vp, vp, vp, vp, vp, vp, vp, ci, ci, ci, ci, ci]),
+        "llmrs_attention_decode_noalloc": (ci, [vp, vp, vp, vp, vp, vp, vp, ci, ci, ci, ci, ci, vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)

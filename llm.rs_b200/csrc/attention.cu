@@ -18,6 +18,8 @@
 // q.k partial dots with a transposing butterfly (31 shuffles per 32 dots),
 // run an online softmax and accumulate V.  Split partials (m, l, acc) go to
 // global memory; the last CTA of each KV head merges them in split order.
+#include <mutex>
+
 #include "attention.cuh"
 #include "common.cuh"
 
@@ -434,4 +436,93 @@ int attention_decode_launch(const AttnParams &p, cudaStream_t stream, bool pdl)
     return fail(LLMRS_ENOTSUP, "attention: head_dim %d with n_rep %d not supported", p.head_dim, nrep);
 }
 
+// ----------------------------------------------------------------------------
+// Allocation-free variant.  Some callers cannot allocate device memory: their
+// device memory belongs to another allocator that must account for every byte
+// (a serving runtime's pre-reserved pool), or they must not allocate after
+// start-up, or they cannot create an llmrs_ctx (which allocates).  For them
+// the split partials, the KV-head tickets and an error word live in this fixed
+// array, linked into the library: every GPU that loads the library holds it
+// until the process exits.
+constexpr size_t NOALLOC_HEADER = 1024;                        // tickets + error word
+constexpr size_t NOALLOC_BYTES = NOALLOC_HEADER + (2u << 20);  // + 2 MiB of split partials
+constexpr int NOALLOC_MAX_KV = 128;                            // tickets that fit the header
+static __device__ __align__(256) unsigned char g_attn_scratch[NOALLOC_BYTES];
+
+namespace {
+std::mutex g_noalloc_mu;
+unsigned char *g_noalloc_ptr[256];   // device address of g_attn_scratch, per device
+bool g_noalloc_ready[256];
+
+// Once per device, with that device current: resolve the array's device
+// address (the host-side name is only a stand-in) and set kernel attributes.
+int noalloc_setup(int device, unsigned char **out)
+{
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (device < 0 || device >= 256)
+        return fail(LLMRS_EINVAL, "device ordinal %d out of range", device);
+    if (!g_noalloc_ready[device]) {
+        unsigned char *ptr = nullptr;
+        cudaError_t e = cudaGetSymbolAddress((void **)&ptr, g_attn_scratch);
+        if (e != cudaSuccess)
+            return fail(LLMRS_ECUDA, "cudaGetSymbolAddress(scratch): %s", cudaGetErrorString(e));
+        LLMRS_TRY(attention_prepare());
+        g_noalloc_ptr[device] = ptr;
+        g_noalloc_ready[device] = true;
+    }
+    *out = g_noalloc_ptr[device];
+    return LLMRS_OK;
+}
+} // namespace
+
 } // namespace llmrs
+
+using namespace llmrs;
+
+extern "C" int llmrs_attention_decode_noalloc(void *cuda_stream, const float *d_qkv, float *d_kcache,
+                                              float *d_vcache, const float *d_rope_cos, const float *d_rope_sin,
+                                              float *d_out, int n_heads, int n_kv_heads, int head_dim, int max_seq,
+                                              int pos, unsigned int *d_err)
+{
+    LLMRS_CHECK_ARG(d_qkv && d_kcache && d_vcache && d_rope_cos && d_rope_sin && d_out, "NULL argument");
+    LLMRS_CHECK_ARG(n_kv_heads > 0 && n_heads > 0 && n_heads % n_kv_heads == 0, "bad head counts %d/%d", n_heads,
+                    n_kv_heads);
+    LLMRS_CHECK_ARG(max_seq > 0 && pos >= 0 && pos < max_seq, "position %d outside [0,%d)", pos, max_seq);
+    const int n_splits = attention_default_splits(n_kv_heads);
+    const size_t part_bytes = attention_partials_floats(n_heads, head_dim, n_splits) * sizeof(float);
+    LLMRS_CHECK_ARG(n_kv_heads <= NOALLOC_MAX_KV,
+                    "attention_decode_noalloc: %d KV heads exceed the fixed scratch limit of %d", n_kv_heads,
+                    NOALLOC_MAX_KV);
+    LLMRS_CHECK_ARG(part_bytes <= NOALLOC_BYTES - NOALLOC_HEADER,
+                    "attention_decode_noalloc: %zu bytes of split partials exceed the fixed scratch of %zu bytes "
+                    "(%d heads x %d splits x head_dim %d)",
+                    part_bytes, (size_t)(NOALLOC_BYTES - NOALLOC_HEADER), n_heads, n_splits, head_dim);
+    int device = 0;
+    LLMRS_CUDA_TRY(cudaGetDevice(&device));
+    unsigned char *scratch = nullptr;
+    LLMRS_TRY(noalloc_setup(device, &scratch));
+    cudaStream_t stream = reinterpret_cast<cudaStream_t>(cuda_stream);
+    unsigned int *tickets = reinterpret_cast<unsigned int *>(scratch);
+    unsigned int *own_err = tickets + NOALLOC_MAX_KV;
+    // tickets must start at zero (a previous call that was cut short may have left counts)
+    LLMRS_CUDA_TRY(cudaMemsetAsync(tickets, 0, (size_t)(NOALLOC_MAX_KV + 1) * sizeof(unsigned int), stream));
+    AttnParams a{};
+    a.n_heads = n_heads;
+    a.n_kv = n_kv_heads;
+    a.head_dim = head_dim;
+    a.max_seq = max_seq;
+    a.n_splits = n_splits;
+    a.pos_fixed = pos;
+    a.qkv = d_qkv;
+    a.kc = d_kcache;
+    a.vc = d_vcache;
+    a.rope_cos = d_rope_cos;
+    a.rope_sin = d_rope_sin;
+    a.ctx = d_out;
+    a.err = d_err ? d_err : own_err;
+    a.inv_sqrt_d = 1.0f / sqrtf((float)head_dim);
+    a.part = reinterpret_cast<float *>(scratch + NOALLOC_HEADER);
+    a.counter = tickets;
+    return attention_decode_launch(a, stream, false);
+}
+
