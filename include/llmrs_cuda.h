@@ -223,6 +223,12 @@ int llmrs_model_decode_kernel_count(llmrs_model *model, int *count);
  * (0 QKV GEMV, 1 attention, 2 o_proj GEMV, 3 gate_up GEMV, 4 down GEMV,
  * 5 LM head GEMV) for i < *n (in: capacity, out: kernels run) */
 int llmrs_model_profile_decode(llmrs_model *model, int token, int pos, float *ms_out, int *kind_out, int *n);
+/* run one decode step through a traced copy of the step graph (same launches,
+ * same programmatic overlap) and return a device timeline: for kernel i,
+ * h_marks[3i] = first CTA start, [3i+1] = first CTA past its wait on the previous
+ * kernel, [3i+2] = last CTA end (globaltimer ns); kinds[i] as in profile_decode.
+ * *n: in = capacity (kernels), out = kernels of the step */
+int llmrs_model_trace_decode(llmrs_model *model, int token, int pos, unsigned long long *h_marks, int *kinds, int *n);
 /* time `iters` device-resident decode steps (graph replays) with CUDA events
  * on the model's stream; *ms_total = elapsed ms; the KV position advances */
 int llmrs_model_time_decode(llmrs_model *model, int token, int pos, int iters, float *ms_total);

@@ -40,7 +40,7 @@ EXPORTS = [
     "llmrs_model_set_weight", "llmrs_kv_fill", "llmrs_kv_fill_synthetic", "llmrs_kv_read",
     "llmrs_decode_step", "llmrs_generate", "llmrs_prefill", "llmrs_model_logits", "llmrs_rope_table",
     "llmrs_model_decode_kernel_count", "llmrs_model_time_decode", "llmrs_model_profile_decode",
-    "llmrs_attention_decode", "llmrs_attention_decode_noalloc",
+    "llmrs_attention_decode", "llmrs_attention_decode_noalloc", "llmrs_model_trace_decode",
 ]
 
 
@@ -123,6 +123,7 @@ def lib():
         "llmrs_model_profile_decode": (ci, [vp, ci, ci, vp, vp, ip]),
         "llmrs_attention_decode": (ci, [vp, vp, vp, vp, vp, vp, vp, ci, ci, ci, ci, ci]),
         "llmrs_attention_decode_noalloc": (ci, [vp, vp, vp, vp, vp, vp, vp, ci, ci, ci, ci, ci, vp]),
+        "llmrs_model_trace_decode": (ci, [vp, ci, ci, vp, vp, ip]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -447,6 +448,18 @@ class Model:
         check(lib().llmrs_model_profile_decode(self.h, int(token), int(pos), _ptr(ms), _ptr(kinds),
                                                ctypes.byref(n)))
         return [(self.KERNEL_KINDS[k], float(t)) for k, t in zip(kinds[:n.value], ms[:n.value])]
+
+    def trace_decode(self, token, pos):
+        """Device timeline of one graph-launched decode step: list of
+        (kind, start_ns, go_ns, end_ns) relative to the first kernel's start."""
+        cap = self.decode_kernel_count()
+        marks = np.zeros(3 * cap, np.uint64)
+        kinds = np.zeros(cap, np.int32)
+        n = ctypes.c_int(cap)
+        check(lib().llmrs_model_trace_decode(self.h, int(token), int(pos), _ptr(marks), _ptr(kinds), ctypes.byref(n)))
+        marks = marks[:3 * n.value].reshape(-1, 3).astype(np.int64)
+        t0 = int(marks[0, 0])
+        return [(self.KERNEL_KINDS[k], int(a - t0), int(b - t0), int(c - t0)) for k, (a, b, c) in zip(kinds, marks)]
 
     def time_decode(self, token, pos, iters):
         ms = ctypes.c_float(0)

@@ -116,6 +116,7 @@ __global__ void __launch_bounds__(ATHREADS) attn_decode_kernel(const AttnParams 
             mbar_init(&empty[s], CWARPS);
         }
         fence_mbar_init();
+        trace_start(p.trace, p.trace_slot);
     }
     __syncthreads();
 
@@ -140,6 +141,8 @@ __global__ void __launch_bounds__(ATHREADS) attn_decode_kernel(const AttnParams 
 
     // ------------------------------------------------------------ consumers
     griddep_wait();
+    if (threadIdx.x == 0)
+        trace_go(p.trace, p.trace_slot);
     if (!pos_ok) {
         if (threadIdx.x == 0)
             atomicCAS(p.err, 0u, (uint32_t)DEV_ERR_BAD_POS);
@@ -318,6 +321,8 @@ __global__ void __launch_bounds__(ATHREADS) attn_decode_kernel(const AttnParams 
     if (ctid == 0)
         s_last = (atomicAdd(&p.counter[g], 1u) == (unsigned)(p.n_splits - 1)) ? 1u : 0u;
     named_bar_sync(1, CWARPS * 32);
+    if (ctid == 0)
+        trace_end(p.trace, p.trace_slot);
     if (!s_last)
         return;
     __threadfence();
@@ -367,8 +372,10 @@ __global__ void __launch_bounds__(ATHREADS) attn_decode_kernel(const AttnParams 
             a += __ldcg(src + (size_t)s * PS) * wsplit[h * p.n_splits + s];
         p.ctx[(size_t)(g * NREP + h) * D + d] = a / ltot[h];
     }
-    if (ctid == 0)
+    if (ctid == 0) {
         p.counter[g] = 0u;
+        trace_end(p.trace, p.trace_slot);
+    }
 }
 
 template <int D, int NREP>

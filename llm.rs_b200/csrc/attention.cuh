@@ -19,6 +19,8 @@ struct AttnParams {
     const StepState *state;  // decode position (nullptr: use pos_fixed)
     int pos_fixed;
     uint32_t *err;
+    unsigned long long *trace; // optional timeline (see GemvParams)
+    int trace_slot;
     int n_heads, n_kv, head_dim, max_seq, n_splits;
     float inv_sqrt_d;        // 1 / sqrt(D), as src/core/layer.rs:258 computes it
 };

@@ -178,6 +178,27 @@ __device__ __forceinline__ void named_bar_sync(int id, int nthreads)
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
+// Timeline marks of a traced decode step (globaltimer ns), three per kernel:
+// [3*slot] first CTA start, [3*slot+1] first CTA past griddepcontrol.wait,
+// [3*slot+2] last CTA end.
+__device__ __forceinline__ void trace_start(unsigned long long *trace, int slot)
+{
+    if (trace)
+        atomicMin(&trace[3 * slot], (unsigned long long)globaltimer_ns());
+}
+
+__device__ __forceinline__ void trace_go(unsigned long long *trace, int slot)
+{
+    if (trace)
+        atomicMin(&trace[3 * slot + 1], (unsigned long long)globaltimer_ns());
+}
+
+__device__ __forceinline__ void trace_end(unsigned long long *trace, int slot)
+{
+    if (trace)
+        atomicMax(&trace[3 * slot + 2], (unsigned long long)globaltimer_ns());
+}
+
 // order-preserving key for a float + lowest-index tie break (max of keys = argmax)
 __device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t idx)
 {

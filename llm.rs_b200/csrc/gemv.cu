@@ -362,6 +362,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         for (int w = 0; w < NW; w++)
             mbar_init(&link[w], 1);
         fence_mbar_init();
+        trace_start(p.trace, p.trace_slot);
     }
     __syncthreads();
 
@@ -395,6 +396,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     LLMRS_TRACE_END(1);
     LLMRS_TRACE_BEGIN(2);
     const int ctid = threadIdx.x;
+    if (ctid == 0)
+        trace_go(p.trace, p.trace_slot);
     load_activation<WF, PRO>(p, act, act_s, act_c, red, ctid, PRO_THREADS, 1);
     named_bar_sync(1, PRO_THREADS);
     LLMRS_TRACE_END(2);
@@ -515,6 +518,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     if (EPI == EPI_ARGMAX)
         argmax_finalize(p, best, ctid, PRO_THREADS, 1);
     LLMRS_TRACE_FLUSH(0);
+    if (ctid == 0)
+        trace_end(p.trace, p.trace_slot);
 }
 
 // ------------------------------------------------------------------ fallback

@@ -56,6 +56,8 @@ struct GemvParams {
     int n_stages;          // set by gemv_launch from the plan
     int box_rows;
     int rows_per_cta;
+    unsigned long long *trace; // optional timeline marks, 3 per kernel (see trace_start)
+    int trace_slot;
 };
 
 // Launch geometry + TMA descriptors of one weight matrix, built once per weight.

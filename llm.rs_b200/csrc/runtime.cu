@@ -139,8 +139,10 @@ struct llmrs_model {
     int log_cap = 0;
     int n_splits = 1;
     int kernels_per_step = 0;
-    // graph of one decode step
+    // graph of one decode step (and a copy that records a device timeline)
     cudaGraphExec_t graph = nullptr;
+    cudaGraphExec_t graph_traced = nullptr;
+    unsigned long long *d_trace = nullptr; // 3 marks per kernel
     // pinned host staging
     int *h_stage = nullptr; // 13 slots of 4 ints (token, pos) for H2D; [60..61]: next token, err
     int h_stage_n = 0;
@@ -489,6 +491,8 @@ static void model_free(llmrs_model *m)
         return;
     if (m->graph)
         cudaGraphExecDestroy(m->graph);
+    if (m->graph_traced)
+        cudaGraphExecDestroy(m->graph_traced);
     if (m->arena.base)
         cudaFree(m->arena.base);
     if (m->h_stage)
@@ -535,6 +539,7 @@ int llmrs_model_create(llmrs_ctx *ctx, const llmrs_config *cfg, llmrs_model **ou
     total += ((size_t)H + qkv_rows + qdim + F + V) * 4 + 5 * 256;           // activations
     total += attention_partials_floats(m->Hq, D, m->n_splits) * 4 + 256;
     total += (size_t)m->Hkv * 4 + sizeof(StepState) + (size_t)m->log_cap * 4 + 1024;
+    total += (size_t)3 * (5 * cfg->n_layers + 8) * 8 + 256; // timeline marks
     cudaError_t e = cudaMalloc(&m->arena.base, total);
     if (e != cudaSuccess) {
         model_free(m);
@@ -582,7 +587,8 @@ int llmrs_model_create(llmrs_ctx *ctx, const llmrs_config *cfg, llmrs_model **ou
     m->att_counter = (unsigned int *)A.take((size_t)m->Hkv * 4);
     m->state = (StepState *)A.take(sizeof(StepState));
     m->token_log = (int *)A.take((size_t)m->log_cap * 4);
-    if (!m->token_log) {
+    m->d_trace = (unsigned long long *)A.take((size_t)3 * (5 * cfg->n_layers + 8) * 8);
+    if (!m->token_log || !m->d_trace) {
         model_free(m);
         return fail(LLMRS_ENOMEM, "model arena layout overflow");
     }
@@ -833,8 +839,9 @@ struct KernelTimer {
     }
 };
 
-static int enqueue_step(llmrs_model *m, cudaStream_t s, KernelTimer *kt = nullptr)
+static int enqueue_step(llmrs_model *m, cudaStream_t s, KernelTimer *kt = nullptr, unsigned long long *trace = nullptr)
 {
+    int slot = 0;
     // with a timer every kernel is bracketed by events and launched without
     // programmatic overlap, so each event pair times exactly one kernel
     const bool overlap = kt == nullptr;
@@ -856,6 +863,8 @@ static int enqueue_step(llmrs_model *m, cudaStream_t s, KernelTimer *kt = nullpt
         p.norm_w = L.attn_norm;
         p.y = m->qkv;
         p.state = m->state;
+        p.trace = trace;
+        p.trace_slot = slot++;
         int pro = PRO_NORM;
         if (l == 0) {
             pro = PRO_EMBED_NORM;
@@ -884,6 +893,8 @@ static int enqueue_step(llmrs_model *m, cudaStream_t s, KernelTimer *kt = nullpt
         a.max_seq = m->S;
         a.n_splits = m->n_splits;
         a.inv_sqrt_d = 1.0f / sqrtf((float)m->D);
+        a.trace = trace;
+        a.trace_slot = slot++;
         LLMRS_TRY(mark(1));
         LLMRS_TRY(attention_decode_launch(a, s, overlap));
         LLMRS_TRY(mark(-1));
@@ -897,6 +908,8 @@ static int enqueue_step(llmrs_model *m, cudaStream_t s, KernelTimer *kt = nullpt
         o.x = m->ctxv;
         o.y = m->x;
         o.residual = m->x;
+        o.trace = trace;
+        o.trace_slot = slot++;
         LLMRS_TRY(mark(2));
         LLMRS_TRY(gemv_launch(L.o.plan, o, PRO_F32, EPI_RESIDUAL, s, overlap));
         LLMRS_TRY(mark(-1));
@@ -911,6 +924,8 @@ static int enqueue_step(llmrs_model *m, cudaStream_t s, KernelTimer *kt = nullpt
         g.x = m->x;
         g.norm_w = L.mlp_norm;
         g.y = m->act;
+        g.trace = trace;
+        g.trace_slot = slot++;
         LLMRS_TRY(mark(3));
         LLMRS_TRY(gemv_launch(L.gate_up.plan, g, PRO_NORM, EPI_SILU, s, overlap));
         LLMRS_TRY(mark(-1));
@@ -924,6 +939,8 @@ static int enqueue_step(llmrs_model *m, cudaStream_t s, KernelTimer *kt = nullpt
         d.x = m->act;
         d.y = m->x;
         d.residual = m->x;
+        d.trace = trace;
+        d.trace_slot = slot++;
         LLMRS_TRY(mark(4));
         LLMRS_TRY(gemv_launch(L.down.plan, d, PRO_F32, EPI_RESIDUAL, s, overlap));
         LLMRS_TRY(mark(-1));
@@ -941,20 +958,20 @@ static int enqueue_step(llmrs_model *m, cudaStream_t s, KernelTimer *kt = nullpt
     h.y = m->logits;
     h.state = m->state;
     h.token_log = m->token_log;
+    h.trace = trace;
+    h.trace_slot = slot++;
     LLMRS_TRY(mark(5));
     LLMRS_TRY(gemv_launch(m->lm_head.plan, h, PRO_NORM, EPI_ARGMAX, s, overlap));
     LLMRS_TRY(mark(-1));
     return LLMRS_OK;
 }
 
-static int ensure_graph(llmrs_model *m)
+static int capture_step(llmrs_model *m, cudaGraphExec_t *out, unsigned long long *trace)
 {
-    if (m->graph)
-        return LLMRS_OK;
     cudaStream_t s = m->ctx->stream;
     cudaGraph_t g = nullptr;
     LLMRS_CUDA_TRY(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
-    int rc = enqueue_step(m, s);
+    int rc = enqueue_step(m, s, nullptr, trace);
     cudaError_t e = cudaStreamEndCapture(s, &g);
     if (rc != LLMRS_OK) {
         if (g)
@@ -963,13 +980,20 @@ static int ensure_graph(llmrs_model *m)
     }
     if (e != cudaSuccess)
         return fail(LLMRS_ECUDA, "graph capture: %s", cudaGetErrorString(e));
-    e = cudaGraphInstantiate(&m->graph, g, 0);
+    e = cudaGraphInstantiate(out, g, 0);
     cudaGraphDestroy(g);
     if (e != cudaSuccess) {
-        m->graph = nullptr;
+        *out = nullptr;
         return fail(LLMRS_ECUDA, "graph instantiate: %s", cudaGetErrorString(e));
     }
     return LLMRS_OK;
+}
+
+static int ensure_graph(llmrs_model *m)
+{
+    if (m->graph)
+        return LLMRS_OK;
+    return capture_step(m, &m->graph, nullptr);
 }
 
 static int check_state_err(llmrs_model *m, uint32_t e)
@@ -1112,6 +1136,37 @@ int llmrs_model_profile_decode(llmrs_model *m, int token, int pos, float *ms_out
     LLMRS_TRY(rc);
     if (e != cudaSuccess)
         return fail(LLMRS_ECUDA, "profile: %s", cudaGetErrorString(e));
+    uint32_t err = 0;
+    LLMRS_CUDA_TRY(cudaMemcpy(&err, &m->state->err, 4, cudaMemcpyDeviceToHost));
+    return check_state_err(m, err);
+}
+
+int llmrs_model_trace_decode(llmrs_model *m, int token, int pos, unsigned long long *h_marks, int *kinds, int *n)
+{
+    LLMRS_CHECK_ARG(m && h_marks && kinds && n, "NULL argument");
+    LLMRS_CHECK_ARG(token >= 0 && token < m->V && pos >= 0 && pos < m->S, "token/position out of range");
+    const int nk = m->kernels_per_step;
+    LLMRS_CHECK_ARG(*n >= nk, "marks buffer holds %d kernels, the step launches %d", *n, nk);
+    cudaSetDevice(m->ctx->device);
+    if (!m->graph_traced)
+        LLMRS_TRY(capture_step(m, &m->graph_traced, m->d_trace));
+    cudaStream_t s = m->ctx->stream;
+    std::vector<unsigned long long> init((size_t)3 * nk);
+    for (int i = 0; i < nk; i++) {
+        init[3 * i] = ~0ull;
+        init[3 * i + 1] = ~0ull;
+        init[3 * i + 2] = 0ull;
+    }
+    LLMRS_CUDA_TRY(cudaMemcpyAsync(m->d_trace, init.data(), init.size() * 8, cudaMemcpyHostToDevice, s));
+    LLMRS_TRY(set_token_pos(m, token, pos, 0));
+    LLMRS_CUDA_TRY(cudaGraphLaunch(m->graph_traced, s));
+    LLMRS_CUDA_TRY(cudaMemcpyAsync(h_marks, m->d_trace, init.size() * 8, cudaMemcpyDeviceToHost, s));
+    LLMRS_CUDA_TRY(cudaStreamSynchronize(s));
+    for (int l = 0; l < m->cfg.n_layers; l++)
+        for (int k = 0; k < 5; k++)
+            kinds[5 * l + k] = k;
+    kinds[nk - 1] = 5;
+    *n = nk;
     uint32_t err = 0;
     LLMRS_CUDA_TRY(cudaMemcpy(&err, &m->state->err, 4, cudaMemcpyDeviceToHost));
     return check_state_err(m, err);
