@@ -9,15 +9,18 @@
 // row is read from HBM once (the reference replicates K/V per query head,
 // src/core/loader.rs:62-98; the values are identical).
 //
-// Split-K (flash-decoding): grid = n_splits x n_kv.  A producer warp streams
-// 32-position K and V tiles of its split into a shared-memory ring with bulk
-// TMA copies; the cache rows it reads were written by earlier steps, so it
-// starts before griddepcontrol.wait (the first kernel of every decode step is
-// launched without programmatic overlap, so `pos` is stable for the whole
-// step).  Four consumer warps take 8 positions of each tile, reduce the
-// q.k partial dots with a transposing butterfly (31 shuffles per 32 dots),
-// run an online softmax and accumulate V.  Split partials (m, l, acc) go to
-// global memory; the last CTA of each KV head merges them in split order.
+// Split-K (flash-decoding): grid = n_splits x n_kv, one CTA per SM.  Each of
+// the CTA's 12 (D = 128) or 16 (D = 64) warps owns every NW-th 8-position
+// chunk of the split and a private 2-slot shared-memory ring that its lane 0
+// fills with bulk copies of K and V rows; the cached rows were written by
+// earlier steps, so the first two chunks per warp are requested before
+// griddepcontrol.wait (the first kernel of every decode step is launched
+// without programmatic overlap, so `pos` is stable for the whole step).  A
+// warp reduces the q.k partial dots of a chunk with a transposing butterfly
+// (31 shuffles per 32 dots), runs an online softmax and accumulates V; the
+// warps of a CTA merge through shared memory, split partials (m, l, acc) go
+// to global memory, and the last CTA of each KV head merges them in split
+// order.
 #include <mutex>
 
 #include "attention.cuh"
@@ -27,14 +30,58 @@ namespace llmrs {
 
 namespace {
 
-constexpr int TILE = 32;   // positions per stage
-constexpr int CWARPS = 4;  // consumer warps
-// 3 stages for n_rep 4 (keeps ~106 KB so a PDL-prefetching GEMV CTA fits beside it); 2 for n_rep 8
-template <int NREP>
-struct AttnStages {
-    static constexpr int value = NREP >= 8 ? 2 : 3;
+constexpr int CH = 8; // positions per chunk: one warp's unit of work
+
+// Phase marks for an instrumented build (no-ops here): 0 entry, 1 q staged,
+// 2 first chunk landed, 3 chunk loop done, 4 warps merged, 5 ticket taken,
+// 6 split merge done, 7 last warp's loop done.
+#ifndef LLMRS_ATTN_MARK
+#define LLMRS_ATTN_MARK(ev)
+#define LLMRS_ATTN_MARK_MAX(ev)
+#endif
+
+// Consumer warps per CTA.  Each warp owns a private 2-slot ring of CH-position
+// K|V chunks (loaded by its own lane 0 with bulk copies, one mbarrier per
+// slot), so warps never wait on each other until the end-of-split merge and
+// a slot's barrier is only ever awaited by the warp that consumed its
+// previous phase (no parity aliasing).  The ring fills the shared memory:
+// 12 warps x 2 x 8 KB at D = 128, 16 x 2 x 4 KB at D = 64.
+template <int D>
+struct AttnWarps {
+    static constexpr int value = D >= 128 ? 12 : 16;
 };
-constexpr int ATHREADS = (CWARPS + 1) * 32;
+
+// K chunk in shared memory: the 3-D box [D/32 segments][CH rows][32 floats]
+// with the 128-byte swizzle (16-byte unit u of 128-byte line L lands at unit
+// u ^ (L % 8)), so lanes reading the same columns of 8 different rows hit 8
+// different bank groups.  Float index of (row r, column d):
+template <int CHR>
+__device__ __forceinline__ int kswz(int r, int d)
+{
+    const int line = (d >> 5) * CHR + r;
+    return line * 32 + ((((d >> 2) & 7) ^ (line & 7)) << 2) + (d & 3);
+}
+
+template <int D, int NREP>
+struct AttnLayout {
+    static constexpr int NW = AttnWarps<D>::value;
+    static constexpr int ROWB = D * 4;           // bytes per cache row
+    static constexpr int KBYTES = CH * ROWB;     // swizzled K box (multiple of 1024)
+    static constexpr int SLOT = 2 * KBYTES;      // K box, then CH plain V rows
+    static constexpr int RING = 2 * SLOT;        // per warp
+    static constexpr int QS = D + 4;             // padded q row: NREP heads in distinct banks
+    static constexpr size_t q_off = (size_t)NW * RING;                        // [NREP][QS]
+    static constexpr size_t probs_off = q_off + (size_t)NREP * QS * 4;        // [NW][CH*NREP]
+    static constexpr size_t wm_off = probs_off + (size_t)NW * CH * NREP * 4; // [NW][NREP]
+    static constexpr size_t wl_off = wm_off + (size_t)NW * NREP * 4;        // [NW][NREP]
+    static constexpr size_t fw_off = wl_off + (size_t)NW * NREP * 4;        // [NW][NREP]
+    static constexpr size_t tot_off = fw_off + (size_t)NW * NREP * 4;       // [2][NREP]
+    static constexpr size_t bar_off = (tot_off + 2 * NREP * 4 + 7) / 8 * 8; // [NW][2]
+    static constexpr size_t merge_bar_off = bar_off + (size_t)NW * 2 * 8;
+    static constexpr size_t bytes = merge_bar_off + 8 + 1024; // + 1024-byte alignment slack
+    static_assert(NREP * D * 4 <= RING, "a warp's partial accumulator must fit its ring");
+    static_assert(KBYTES % 1024 == 0 && CH == 8, "swizzled K boxes must stay 1024-byte aligned");
+};
 
 // v[j] holds lane-partial sums of 32 dot products; on return lane i holds the
 // full sum of dot product i.
@@ -53,10 +100,25 @@ __device__ __forceinline__ float butterfly32(float (&v)[32], int lane)
     return v[0];
 }
 
-// rotate-half RoPE of one head held DL values per lane (lane l: dims l*DL..),
-// exact reference arithmetic: x[j]*cos - x[j+mid]*sin ; x[j]*sin + x[j+mid]*cos
+// cos/sin table values this lane needs for rotate-half RoPE (lane l holds
+// dims l*DL.., frequency index (l % 16)*DL + k)
 template <int D>
-__device__ __forceinline__ void rope_lane(float (&x)[D / 32], int lane, const float *cosr, const float *sinr)
+__device__ __forceinline__ void rope_table_lane(float (&c)[D / 32], float (&s)[D / 32], int lane, const float *cosr,
+                                                const float *sinr)
+{
+    constexpr int DL = D / 32;
+#pragma unroll
+    for (int k = 0; k < DL; k++) {
+        c[k] = cosr[(lane & 15) * DL + k];
+        s[k] = sinr[(lane & 15) * DL + k];
+    }
+}
+
+// rotate-half RoPE of one head held DL values per lane, exact reference
+// arithmetic: x[j]*cos - x[j+mid]*sin ; x[j]*sin + x[j+mid]*cos
+template <int D>
+__device__ __forceinline__ void rope_lane(float (&x)[D / 32], int lane, const float (&c)[D / 32],
+                                          const float (&s)[D / 32])
 {
     constexpr int DL = D / 32;
     float other[DL];
@@ -66,100 +128,113 @@ __device__ __forceinline__ void rope_lane(float (&x)[D / 32], int lane, const fl
     const bool upper = lane >= 16;
 #pragma unroll
     for (int k = 0; k < DL; k++) {
-        const int j = (lane & 15) * DL + k; // frequency index 0..D/2-1
-        const float c = cosr[j], s = sinr[j];
         if (!upper)
-            x[k] = __fsub_rn(__fmul_rn(x[k], c), __fmul_rn(other[k], s));
+            x[k] = __fsub_rn(__fmul_rn(x[k], c[k]), __fmul_rn(other[k], s[k]));
         else
-            x[k] = __fadd_rn(__fmul_rn(other[k], s), __fmul_rn(x[k], c));
+            x[k] = __fadd_rn(__fmul_rn(other[k], s[k]), __fmul_rn(x[k], c[k]));
+    }
+}
+
+// DL consecutive floats of a shared-memory row (16- or 8-byte vector load)
+template <int DL>
+__device__ __forceinline__ void lds_lane(float (&r)[DL], const float *src)
+{
+    if constexpr (DL == 4) {
+        const float4 t = *reinterpret_cast<const float4 *>(src);
+        r[0] = t.x; r[1] = t.y; r[2] = t.z; r[3] = t.w;
+    } else if constexpr (DL == 2) {
+        const float2 t = *reinterpret_cast<const float2 *>(src);
+        r[0] = t.x; r[1] = t.y;
+    } else {
+#pragma unroll
+        for (int k = 0; k < DL; k++)
+            r[k] = src[k];
     }
 }
 
 template <int D, int NREP>
-__global__ void __launch_bounds__(ATHREADS) attn_decode_kernel(const AttnParams p)
+__global__ void __launch_bounds__(AttnWarps<D>::value * 32, 1) attn_decode_kernel(const __grid_constant__ AttnParams p)
 {
     static_assert(NREP == 4 || NREP == 8, "n_rep must be 4 or 8");
-    constexpr int NSTAGE = AttnStages<NREP>::value;
+    using Lay = AttnLayout<D, NREP>;
+    constexpr int NW = Lay::NW;
+    constexpr int NT = NW * 32;
     constexpr int DL = D / 32;
-    constexpr int G = 32 / NREP;          // positions per butterfly
-    constexpr int NFLY = 8 / G;           // butterflies per warp per tile (8 positions)
-    constexpr int ROWB = D * 4;           // bytes per cache row
-    constexpr int STAGE = 2 * TILE * ROWB;
-    extern __shared__ __align__(128) uint8_t smem[];
-    float *kv_stage = reinterpret_cast<float *>(smem);
-    float *knew = reinterpret_cast<float *>(smem + NSTAGE * STAGE);
-    float *vnew = knew + D;
-    float *wm = vnew + D;                       // [CWARPS][NREP]
-    float *wl = wm + CWARPS * NREP;             // [CWARPS][NREP]
-    float *wacc = wl + CWARPS * NREP;           // [CWARPS][NREP][D]
-    uint64_t *full = reinterpret_cast<uint64_t *>(wacc + CWARPS * NREP * D);
-    uint64_t *empty = full + NSTAGE;
+    constexpr int G = 32 / NREP;   // positions per butterfly
+    constexpr int NFLY = CH / G;   // butterflies per chunk
+    constexpr int ROWB = Lay::ROWB;
+    extern __shared__ __align__(128) uint8_t smem_raw[];
+    uint8_t *smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
+    float *q_s = reinterpret_cast<float *>(smem + Lay::q_off);
+    float *wm = reinterpret_cast<float *>(smem + Lay::wm_off);
+    float *wl = reinterpret_cast<float *>(smem + Lay::wl_off);
+    float *fw = reinterpret_cast<float *>(smem + Lay::fw_off);
+    float *tot = reinterpret_cast<float *>(smem + Lay::tot_off);
     __shared__ unsigned int s_last;
 
     griddep_launch_dependents();
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int split = blockIdx.x, g = blockIdx.y;
+    LLMRS_ATTN_MARK(0);
+    // `pos` was written by the previous step's last kernel, which finished
+    // before this step's first (non-overlapped) kernel began
     const int pos = p.state ? p.state->pos : p.pos_fixed;
     const bool pos_ok = pos >= 0 && pos < p.max_seq;
     const int Lc = pos_ok ? pos : 0;           // cached positions [0, pos)
     const int t0 = (int)(((long long)split * Lc) / p.n_splits);
     const int t1 = (int)(((long long)(split + 1) * Lc) / p.n_splits);
-    const int ntiles = (t1 - t0 + TILE - 1) / TILE;
+    const int nch = (t1 - t0 + CH - 1) / CH;
+    const int mine = warp < nch ? (nch - warp + NW - 1) / NW : 0; // chunks warp, warp+NW, ...
     const bool owner = split == p.n_splits - 1;
-    const float *kbase = p.kc + (size_t)g * p.max_seq * D;
     const float *vbase = p.vc + (size_t)g * p.max_seq * D;
+    uint8_t *ring = smem + (size_t)warp * Lay::RING;
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + Lay::bar_off) + warp * 2;
+    uint64_t *merge_bar = reinterpret_cast<uint64_t *>(smem + Lay::merge_bar_off);
+    float *probs = reinterpret_cast<float *>(smem + Lay::probs_off) + warp * CH * NREP;
 
-    if (threadIdx.x == 0) {
-        for (int s = 0; s < NSTAGE; s++) {
-            mbar_init(&full[s], 1);
-            mbar_init(&empty[s], CWARPS);
+    auto issue = [&](int j, uint64_t pol) { // chunk j of this warp into slot j & 1 (lane 0)
+        const int ta = t0 + (warp + j * NW) * CH;
+        const int rows = min(CH, t1 - ta);
+        uint64_t *bar = &full[j & 1];
+        uint8_t *dst = ring + (j & 1) * Lay::SLOT;
+        // the K box always moves CH rows (rows past the split are ignored;
+        // past the end of the cache they read as zero)
+        mbar_arrive_expect_tx(bar, (uint32_t)(Lay::KBYTES + rows * ROWB));
+        tma_load_3d(dst, &p.tk, 0, g * p.max_seq + ta, 0, bar, pol);
+        bulk_g2s(dst + Lay::KBYTES, vbase + (size_t)ta * D, (uint32_t)(rows * ROWB), bar, pol);
+    };
+    if (lane == 0) {
+        mbar_init(&full[0], 1);
+        mbar_init(&full[1], 1);
+        if (threadIdx.x == 0) {
+            mbar_init(merge_bar, 1);
+            trace_start(p.trace, p.trace_slot);
         }
         fence_mbar_init();
-        trace_start(p.trace, p.trace_slot);
-    }
-    __syncthreads();
-
-    if (warp == CWARPS) {
-        // ---------------------------------------------------------- producer
-        if (lane == 0) {
-            const uint64_t pol = policy_evict_first();
-            for (int it = 0; it < ntiles; it++) {
-                const int s = it % NSTAGE;
-                if (it >= NSTAGE && !mbar_wait(&empty[s], ((it / NSTAGE) - 1) & 1, p.err))
-                    return;
-                const int ta = t0 + it * TILE;
-                const int rows = min(TILE, t1 - ta);
-                mbar_arrive_expect_tx(&full[s], (uint32_t)(2 * rows * ROWB));
-                uint8_t *st = smem + (size_t)s * STAGE;
-                bulk_g2s(st, kbase + (size_t)ta * D, (uint32_t)(rows * ROWB), &full[s], pol);
-                bulk_g2s(st + TILE * ROWB, vbase + (size_t)ta * D, (uint32_t)(rows * ROWB), &full[s], pol);
-            }
-        }
-        return;
     }
 
-    // ------------------------------------------------------------ consumers
     griddep_wait();
-    if (threadIdx.x == 0)
+    if (threadIdx.x == 0) {
         trace_go(p.trace, p.trace_slot);
-    if (!pos_ok) {
-        if (threadIdx.x == 0)
+        if (!pos_ok)
             atomicCAS(p.err, 0u, (uint32_t)DEV_ERR_BAD_POS);
     }
-    const float *cosr = p.rope_cos + (size_t)(pos_ok ? pos : 0) * (D / 2);
-    const float *sinr = p.rope_sin + (size_t)(pos_ok ? pos : 0) * (D / 2);
-    float q[NREP][DL];
-#pragma unroll
-    for (int h = 0; h < NREP; h++) {
-        const float *qh = p.qkv + (size_t)(g * NREP + h) * D + lane * DL;
+    // The few small loads (q, the new k/v, the RoPE row) are issued before
+    // the K/V stream: queued behind it they would wait for most of it.
+    const float *cosr = p.rope_cos + (size_t)Lc * (D / 2);
+    const float *sinr = p.rope_sin + (size_t)Lc * (D / 2);
+    const bool appender = owner && warp == 0;
+    float qv[DL], kk[DL], vv[DL], rc[DL], rs[DL];
+    if (warp < NREP || appender)
+        rope_table_lane<D>(rc, rs, lane, cosr, sinr);
+    if (warp < NREP) {
+        const float *qh = p.qkv + (size_t)(g * NREP + warp) * D + lane * DL;
 #pragma unroll
         for (int k = 0; k < DL; k++)
-            q[h][k] = qh[k];
-        rope_lane<D>(q[h], lane, cosr, sinr);
+            qv[k] = qh[k];
     }
-    if (owner && warp == 0) {
-        float kk[DL], vv[DL];
+    if (appender) {
         const float *kn = p.qkv + (size_t)p.n_heads * D + (size_t)g * D + lane * DL;
         const float *vn = p.qkv + (size_t)(p.n_heads + p.n_kv) * D + (size_t)g * D + lane * DL;
 #pragma unroll
@@ -167,21 +242,34 @@ __global__ void __launch_bounds__(ATHREADS) attn_decode_kernel(const AttnParams 
             kk[k] = kn[k];
             vv[k] = vn[k];
         }
-        rope_lane<D>(kk, lane, cosr, sinr);
+    }
+    __syncthreads(); // small loads issued; barriers initialised
+    if (lane == 0) {
+        const uint64_t pol = policy_evict_first();
+        for (int j = 0; j < 2 && j < mine; j++)
+            issue(j, pol);
+    }
+    __syncwarp();
+    if (warp < NREP) { // RoPE(q) of head `warp` into shared memory
+        rope_lane<D>(qv, lane, rc, rs);
 #pragma unroll
-        for (int k = 0; k < DL; k++) {
-            knew[lane * DL + k] = kk[k];
-            vnew[lane * DL + k] = vv[k];
-            if (pos_ok) {
+        for (int k = 0; k < DL; k++)
+            q_s[warp * Lay::QS + lane * DL + k] = qv[k];
+    }
+    if (appender) { // RoPE the new key, append k/v at `pos`
+        rope_lane<D>(kk, lane, rc, rs);
+        if (pos_ok) {
+#pragma unroll
+            for (int k = 0; k < DL; k++) {
                 p.kc[((size_t)g * p.max_seq + pos) * D + lane * DL + k] = kk[k];
                 p.vc[((size_t)g * p.max_seq + pos) * D + lane * DL + k] = vv[k];
             }
         }
     }
-    named_bar_sync(1, CWARPS * 32);
+    __syncthreads(); // q_s complete
+    LLMRS_ATTN_MARK(1);
 
-    const int myh = lane % NREP; // head whose softmax state this lane tracks
-    float m_run = -INFINITY, l_run = 0.0f;
+    float m_run = -INFINITY, l_run = 0.0f; // softmax state of head lane % NREP
     float acc[NREP][DL];
 #pragma unroll
     for (int h = 0; h < NREP; h++)
@@ -189,33 +277,44 @@ __global__ void __launch_bounds__(ATHREADS) attn_decode_kernel(const AttnParams 
         for (int k = 0; k < DL; k++)
             acc[h][k] = 0.0f;
 
-    // one tile step over 8 positions held at krow(pp)/vrow(pp); valid(pp) masks
+    // one chunk: positions 0..nvalid-1 of kt (K rows) / vt (V rows)
     auto process = [&](const float *kt, const float *vt, int nvalid) {
+        // scores: lane owns (row b*G + lane/NREP, head lane%NREP) and sums
+        // q[d]*k[d] for d = 0..D-1 in order, unfused, like the reference's
+        // f32 dot (src/backend/cpu.rs:458-551, non-aarch64 branch), then
+        // scales by 1/sqrt(D) (src/core/layer.rs:258): bit-exact scores
         float sc[NFLY];
+        {
+            const float *qh = q_s + (lane % NREP) * Lay::QS;
+            int roff[NFLY], rx[NFLY];
+            float dot[NFLY];
 #pragma unroll
-        for (int b = 0; b < NFLY; b++) {
-            float v[32];
+            for (int b = 0; b < NFLY; b++) {
+                const int r = b * G + lane / NREP;
+                roff[b] = r * 32;
+                rx[b] = r & 7;
+                dot[b] = 0.0f;
+            }
 #pragma unroll
-            for (int pp = 0; pp < G; pp++) {
-                const int pl = b * G + pp;
-                float kr[DL];
+            for (int d4 = 0; d4 < D / 4; d4++) {
+                const float4 qv = *reinterpret_cast<const float4 *>(qh + d4 * 4);
 #pragma unroll
-                for (int k = 0; k < DL; k++)
-                    kr[k] = pl < nvalid ? kt[pl * D + lane * DL + k] : 0.0f;
-#pragma unroll
-                for (int h = 0; h < NREP; h++) {
-                    float d = 0.0f;
-#pragma unroll
-                    for (int k = 0; k < DL; k++)
-                        d = fmaf(q[h][k], kr[k], d);
-                    v[pp * NREP + h] = d;
+                for (int b = 0; b < NFLY; b++) {
+                    const float4 kv = *reinterpret_cast<const float4 *>(
+                        kt + (d4 >> 3) * (CH * 32) + roff[b] + (((d4 & 7) ^ rx[b]) << 2));
+                    float t = dot[b];
+                    t = __fadd_rn(t, __fmul_rn(qv.x, kv.x));
+                    t = __fadd_rn(t, __fmul_rn(qv.y, kv.y));
+                    t = __fadd_rn(t, __fmul_rn(qv.z, kv.z));
+                    t = __fadd_rn(t, __fmul_rn(qv.w, kv.w));
+                    dot[b] = t;
                 }
             }
-            const float s = butterfly32(v, lane) * p.inv_sqrt_d;
-            const int pl = b * G + lane / NREP;
-            sc[b] = pl < nvalid ? s : -INFINITY;
+#pragma unroll
+            for (int b = 0; b < NFLY; b++)
+                sc[b] = (b * G + lane / NREP) < nvalid ? __fmul_rn(dot[b], p.inv_sqrt_d) : -INFINITY;
         }
-        // per-head max over this warp's 8 positions
+        // lane holds (position b*G + lane/NREP, head lane%NREP) for each b
         float tmax = sc[0];
 #pragma unroll
         for (int b = 1; b < NFLY; b++)
@@ -225,19 +324,18 @@ __global__ void __launch_bounds__(ATHREADS) attn_decode_kernel(const AttnParams 
             tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, o));
         const float m_new = fmaxf(m_run, tmax);
         const float corr = (m_run == -INFINITY) ? 0.0f : expf(m_run - m_new);
-        float pr[NFLY];
         float psum = 0.0f;
 #pragma unroll
         for (int b = 0; b < NFLY; b++) {
-            pr[b] = (sc[b] == -INFINITY) ? 0.0f : expf(sc[b] - m_new);
-            psum += pr[b];
+            const float pr = (sc[b] == -INFINITY) ? 0.0f : expf(sc[b] - m_new);
+            probs[b * 32 + lane] = pr; // index position * NREP + head
+            psum += pr;
         }
 #pragma unroll
         for (int o = NREP; o < 32; o <<= 1)
             psum += __shfl_xor_sync(0xffffffffu, psum, o);
         l_run = l_run * corr + psum;
         m_run = m_new;
-        // rescale and accumulate V for every head
 #pragma unroll
         for (int h = 0; h < NREP; h++) {
             const float ch = __shfl_sync(0xffffffffu, corr, h);
@@ -245,46 +343,61 @@ __global__ void __launch_bounds__(ATHREADS) attn_decode_kernel(const AttnParams 
             for (int k = 0; k < DL; k++)
                 acc[h][k] *= ch;
         }
+        __syncwarp();
 #pragma unroll
-        for (int b = 0; b < NFLY; b++) {
+        for (int pl = 0; pl < CH; pl++) {
+            if (pl < nvalid) {
+                float vr[DL];
+                lds_lane<DL>(vr, vt + pl * D + lane * DL);
+                float ph[NREP];
 #pragma unroll
-            for (int pp = 0; pp < G; pp++) {
-                const int pl = b * G + pp;
-                if (pl < nvalid) {
-                    float vr[DL];
+                for (int h4 = 0; h4 < NREP; h4 += 4) {
+                    const float4 t = *reinterpret_cast<const float4 *>(probs + pl * NREP + h4);
+                    ph[h4] = t.x; ph[h4 + 1] = t.y; ph[h4 + 2] = t.z; ph[h4 + 3] = t.w;
+                }
+#pragma unroll
+                for (int h = 0; h < NREP; h++)
 #pragma unroll
                     for (int k = 0; k < DL; k++)
-                        vr[k] = vt[pl * D + lane * DL + k];
-#pragma unroll
-                    for (int h = 0; h < NREP; h++) {
-                        const float ph = __shfl_sync(0xffffffffu, pr[b], pp * NREP + h);
-#pragma unroll
-                        for (int k = 0; k < DL; k++)
-                            acc[h][k] = fmaf(ph, vr[k], acc[h][k]);
-                    }
-                }
+                        acc[h][k] = fmaf(ph[h], vr[k], acc[h][k]);
             }
         }
+        __syncwarp();
     };
 
     bool ok = true;
-    for (int it = 0; it < ntiles; it++) {
-        const int s = it % NSTAGE;
-        if (ok && !mbar_wait(&full[s], (it / NSTAGE) & 1, p.err))
+    for (int j = 0; j < mine; j++) {
+        const int slot = j & 1;
+        if (ok && !mbar_wait(&full[slot], (uint32_t)((j >> 1) & 1), p.err))
             ok = false;
-        const int rows = min(TILE, t1 - (t0 + it * TILE));
-        const float *st = kv_stage + (size_t)s * (STAGE / 4);
-        const int nvalid = max(0, min(8, rows - warp * 8));
-        if (nvalid > 0)
-            process(st + warp * 8 * D, st + TILE * D + warp * 8 * D, nvalid);
-        __syncwarp();
-        if (lane == 0)
-            mbar_arrive(&empty[s]);
+        if (j == 0)
+            LLMRS_ATTN_MARK(2);
+        if (ok) {
+            const int rows = min(CH, t1 - (t0 + (warp + j * NW) * CH));
+            const float *st = reinterpret_cast<const float *>(ring + slot * Lay::SLOT);
+            process(st, st + Lay::KBYTES / 4, rows);
+        }
+        if (ok && lane == 0 && j + 2 < mine) {
+            fence_proxy_async_smem(); // this warp's reads of the slot precede the refill
+            issue(j + 2, policy_evict_first());
+        }
     }
-    if (owner && warp == 0 && pos_ok)
-        process(knew, vnew, 1);
+    LLMRS_ATTN_MARK(3);
+    LLMRS_ATTN_MARK_MAX(7);
+    if (appender && pos_ok) {
+        // the new position, staged in this warp's (now idle) first slot
+        float *st = reinterpret_cast<float *>(ring);
+#pragma unroll
+        for (int k = 0; k < DL; k++) {
+            st[kswz<CH>(0, lane * DL + k)] = kk[k];
+            st[Lay::KBYTES / 4 + lane * DL + k] = vv[k];
+        }
+        __syncwarp();
+        process(st, st + Lay::KBYTES / 4, 1);
+    }
 
-    // merge the warps of this CTA
+    // merge the warps of this CTA: warp partials at the start of each ring
+    float *wacc = reinterpret_cast<float *>(ring);
     if (lane < NREP) {
         wm[warp * NREP + lane] = m_run;
         wl[warp * NREP + lane] = l_run;
@@ -293,103 +406,126 @@ __global__ void __launch_bounds__(ATHREADS) attn_decode_kernel(const AttnParams 
     for (int h = 0; h < NREP; h++)
 #pragma unroll
         for (int k = 0; k < DL; k++)
-            wacc[(warp * NREP + h) * D + lane * DL + k] = acc[h][k];
-    named_bar_sync(1, CWARPS * 32);
+            wacc[h * D + lane * DL + k] = acc[h][k];
+    __syncthreads();
+    LLMRS_ATTN_MARK(4);
     const int ctid = threadIdx.x;
-    const int PS = D + 2;
-    for (int e = ctid; e < NREP * D; e += CWARPS * 32) {
-        const int h = e / D, d = e % D;
+    if (ctid < NREP) {
+        const int h = ctid;
         float M = -INFINITY;
-        for (int w = 0; w < CWARPS; w++)
+        for (int w = 0; w < NW; w++)
             M = fmaxf(M, wm[w * NREP + h]);
-        float a = 0.0f, l = 0.0f;
-        for (int w = 0; w < CWARPS; w++) {
+        float l = 0.0f;
+        for (int w = 0; w < NW; w++) {
             const float mw = wm[w * NREP + h];
             const float f = (mw == -INFINITY) ? 0.0f : expf(mw - M);
-            a += wacc[(w * NREP + h) * D + d] * f;
+            fw[w * NREP + h] = f;
             l += wl[w * NREP + h] * f;
         }
+        tot[h] = M;
+        tot[NREP + h] = l;
+    }
+    __syncthreads();
+    const int PS = D + 2;
+    for (int e = ctid; e < NREP * D; e += NT) {
+        const int h = e / D, d = e % D;
+        float a = 0.0f;
+#pragma unroll 4
+        for (int w = 0; w < NW; w++)
+            a += reinterpret_cast<const float *>(smem + (size_t)w * Lay::RING)[h * D + d] * fw[w * NREP + h];
         float *dst = p.part + ((size_t)(g * NREP + h) * p.n_splits + split) * PS;
         dst[d] = a;
         if (d == 0) {
-            dst[D] = M;
-            dst[D + 1] = l;
+            dst[D] = tot[h];
+            dst[D + 1] = tot[NREP + h];
         }
     }
     __threadfence();
-    named_bar_sync(1, CWARPS * 32);
+    __syncthreads();
     if (ctid == 0)
         s_last = (atomicAdd(&p.counter[g], 1u) == (unsigned)(p.n_splits - 1)) ? 1u : 0u;
-    named_bar_sync(1, CWARPS * 32);
+    __syncthreads();
+    LLMRS_ATTN_MARK(5);
     if (ctid == 0)
         trace_end(p.trace, p.trace_slot);
     if (!s_last)
         return;
     __threadfence();
-    // Last CTA of this KV head: merge the splits in split order.  First every
-    // (head, split) max / sum is fetched in parallel and turned into weights
-    // in shared memory; then each output element sums its split partials with
-    // all loads in flight together.
-    float *wsplit = wacc; // reuse: [NREP][n_splits] weights, then [NREP] totals
-    float *ltot = wacc + NREP * p.n_splits;
-    for (int e = ctid; e < NREP * p.n_splits; e += CWARPS * 32) {
-        const int h = e / p.n_splits, s = e % p.n_splits;
-        const float *src = p.part + ((size_t)(g * NREP + h) * p.n_splits + s) * PS;
-        wsplit[e] = __ldcg(src + D);               // m_s
-        ltot[NREP + e] = __ldcg(src + D + 1);      // l_s
+    // Last CTA of this KV head: one bulk copy brings every split partial of
+    // its NREP heads ([NREP][n_splits][D + 2], contiguous) into shared memory
+    // (the ring is idle now); the splits are then merged in split order.
+    const int ns = p.n_splits;
+    float *pm = reinterpret_cast<float *>(smem); // [NREP][ns][PS]
+    float *wsplit = pm + NREP * ns * PS;         // [NREP][ns] split weights
+    float *ltot = wsplit + NREP * ns;            // [NREP] softmax denominators
+    if (ctid == 0) {
+        // the partials were written through the generic proxy by other CTAs
+        asm volatile("fence.proxy.async.global;" ::: "memory");
+        const uint32_t bytes = (uint32_t)(NREP * ns * PS * 4);
+        mbar_arrive_expect_tx(merge_bar, bytes);
+        bulk_g2s(pm, p.part + (size_t)g * NREP * ns * PS, bytes, merge_bar, policy_evict_first());
     }
-    named_bar_sync(1, CWARPS * 32);
-    if (ctid < NREP) {
-        const int h = ctid;
+    const bool got = mbar_wait(merge_bar, 0, p.err);
+    if (warp < NREP && got) { // head `warp`: max over splits, weights, denominator
+        const int h = warp;
         float M = -INFINITY;
-        for (int s = 0; s < p.n_splits; s++)
-            M = fmaxf(M, wsplit[h * p.n_splits + s]);
+        for (int sp = lane; sp < ns; sp += 32)
+            M = fmaxf(M, pm[(h * ns + sp) * PS + D]);
+        M = warp_max(M);
         float l = 0.0f;
-        for (int s = 0; s < p.n_splits; s++) {
-            const float ms = wsplit[h * p.n_splits + s];
+        for (int sp = lane; sp < ns; sp += 32) {
+            const float ms = pm[(h * ns + sp) * PS + D];
             const float f = (ms == -INFINITY) ? 0.0f : expf(ms - M);
-            l += ltot[NREP + h * p.n_splits + s] * f;
-            wsplit[h * p.n_splits + s] = f;
+            wsplit[h * ns + sp] = f;
+            l += pm[(h * ns + sp) * PS + D + 1] * f;
         }
-        ltot[h] = l;
+        l = warp_sum(l);
+        if (lane == 0)
+            ltot[h] = l;
     }
-    named_bar_sync(1, CWARPS * 32);
-    for (int e = ctid; e < NREP * D; e += CWARPS * 32) {
+    __syncthreads();
+    for (int e = ctid; e < NREP * D && got; e += NT) {
         const int h = e / D, d = e % D;
-        const float *src = p.part + (size_t)(g * NREP + h) * p.n_splits * PS + d;
+        const float *src = pm + (size_t)h * ns * PS + d;
         float a = 0.0f;
-        int s = 0;
-        for (; s + 8 <= p.n_splits; s += 8) {
-            float v[8];
-#pragma unroll
-            for (int u = 0; u < 8; u++)
-                v[u] = __ldcg(src + (size_t)(s + u) * PS);
-#pragma unroll
-            for (int u = 0; u < 8; u++)
-                a += v[u] * wsplit[h * p.n_splits + s + u];
-        }
-        for (; s < p.n_splits; s++)
-            a += __ldcg(src + (size_t)s * PS) * wsplit[h * p.n_splits + s];
+        for (int sp = 0; sp < ns; sp++)
+            a += src[(size_t)sp * PS] * wsplit[h * ns + sp];
         p.ctx[(size_t)(g * NREP + h) * D + d] = a / ltot[h];
     }
     if (ctid == 0) {
         p.counter[g] = 0u;
         trace_end(p.trace, p.trace_slot);
     }
+    __syncthreads();
+    LLMRS_ATTN_MARK(6);
 }
 
-template <int D, int NREP>
-constexpr size_t attn_smem_bytes()
+// K cache [n_kv * max_seq rows][D] viewed as (x: 32 floats of a 128-byte
+// segment, y: row, z: segment), boxes of CH rows x every segment, swizzled
+int encode_k_map(CUtensorMap *map, const float *kc, int rows, int D)
 {
-    return (size_t)AttnStages<NREP>::value * (2 * TILE * D * 4) +
-           (size_t)(2 * D + 2 * CWARPS * NREP + CWARPS * NREP * D) * 4 + 2 * AttnStages<NREP>::value * 8;
+    auto fn = tensor_map_encoder();
+    if (!fn)
+        return fail(LLMRS_ECUDA, "cuTensorMapEncodeTiled unavailable");
+    LLMRS_CHECK_ARG(((uintptr_t)kc & 15) == 0, "attention: K cache not 16-byte aligned");
+    cuuint64_t dims[3] = {32, (cuuint64_t)rows, (cuuint64_t)(D / 32)};
+    cuuint64_t strides[2] = {(cuuint64_t)D * 4, 128};
+    cuuint32_t box[3] = {32, (cuuint32_t)CH, (cuuint32_t)(D / 32)};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float *>(kc), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return fail(LLMRS_ECUDA, "cuTensorMapEncodeTiled (K cache) failed (%d)", (int)r);
+    return LLMRS_OK;
 }
 
 template <int D, int NREP>
 int launch_attn(const AttnParams &p, cudaStream_t stream, bool pdl)
 {
-    const size_t smem = attn_smem_bytes<D, NREP>();
-    LLMRS_CUDA_TRY(launch(attn_decode_kernel<D, NREP>, dim3(p.n_splits, p.n_kv), dim3(ATHREADS), smem, stream, pdl, p));
+    using Lay = AttnLayout<D, NREP>;
+    LLMRS_CUDA_TRY(launch(attn_decode_kernel<D, NREP>, dim3(p.n_splits, p.n_kv), dim3(Lay::NW * 32), Lay::bytes,
+                          stream, pdl, p));
     return LLMRS_OK;
 }
 
@@ -397,7 +533,7 @@ template <int D, int NREP>
 cudaError_t prepare_attn()
 {
     return cudaFuncSetAttribute(attn_decode_kernel<D, NREP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                (int)attn_smem_bytes<D, NREP>());
+                                (int)AttnLayout<D, NREP>::bytes);
 }
 
 } // namespace
@@ -432,14 +568,21 @@ int attention_decode_launch(const AttnParams &p, cudaStream_t stream, bool pdl)
     LLMRS_CHECK_ARG(p.n_kv > 0 && p.n_heads % p.n_kv == 0, "attention: n_heads %d not a multiple of n_kv %d",
                     p.n_heads, p.n_kv);
     const int nrep = p.n_heads / p.n_kv;
+    const bool known = (p.head_dim == 128 || p.head_dim == 64) && (nrep == 4 || nrep == 8);
+    if (!known)
+        return fail(LLMRS_ENOTSUP, "attention: head_dim %d with n_rep %d not supported", p.head_dim, nrep);
+    LLMRS_CHECK_ARG(((uintptr_t)p.vc & 15) == 0, "attention: V cache not 16-byte aligned");
+    LLMRS_CHECK_ARG(p.n_splits >= 1 && p.n_splits <= 32, "attention: %d splits outside [1, 32]", p.n_splits);
+    AttnParams q = p;
+    LLMRS_TRY(encode_k_map(&q.tk, p.kc, p.n_kv * p.max_seq, p.head_dim));
     if (p.head_dim == 128 && nrep == 4)
-        return launch_attn<128, 4>(p, stream, pdl);
+        return launch_attn<128, 4>(q, stream, pdl);
     if (p.head_dim == 128 && nrep == 8)
-        return launch_attn<128, 8>(p, stream, pdl);
+        return launch_attn<128, 8>(q, stream, pdl);
     if (p.head_dim == 64 && nrep == 4)
-        return launch_attn<64, 4>(p, stream, pdl);
+        return launch_attn<64, 4>(q, stream, pdl);
     if (p.head_dim == 64 && nrep == 8)
-        return launch_attn<64, 8>(p, stream, pdl);
+        return launch_attn<64, 8>(q, stream, pdl);
     return fail(LLMRS_ENOTSUP, "attention: head_dim %d with n_rep %d not supported", p.head_dim, nrep);
 }
 

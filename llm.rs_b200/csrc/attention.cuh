@@ -9,6 +9,7 @@
 namespace llmrs {
 
 struct AttnParams {
+    CUtensorMap tk;          // K cache as [D/32 segments][rows][32 floats], 128B-swizzled boxes (set at launch)
     const float *qkv;        // q [Hq*D] | k [Hkv*D] | v [Hkv*D], pre-RoPE (fused QKV GEMV output)
     float *kc, *vc;          // KV cache [Hkv][S][D] f32, position-major
     const float *rope_cos;   // [S][D/2]

@@ -631,7 +631,9 @@ int launch_one(const GemvPlan &plan, const GemvParams &p0, cudaStream_t stream, 
     return LLMRS_OK;
 }
 
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn()
+} // namespace
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder()
 {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
     static std::once_flag once;
@@ -645,11 +647,13 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn()
     return fn;
 }
 
+namespace {
+
 // 2-D map over `rows` rows of `row_bytes` bytes viewed as `elem`-byte elements
 int encode_2d(CUtensorMap *map, const void *base, int elem, size_t row_bytes, int rows, int box_x, int box_y,
               CUtensorMapSwizzle swizzle)
 {
-    auto fn = encode_fn();
+    auto fn = tensor_map_encoder();
     if (!fn)
         return fail(LLMRS_ECUDA, "cuTensorMapEncodeTiled unavailable");
     const CUtensorMapDataType dt = elem == 2 ? CU_TENSOR_MAP_DATA_TYPE_UINT16 : CU_TENSOR_MAP_DATA_TYPE_UINT32;

@@ -2,6 +2,7 @@
 #pragma once
 
 #include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -81,5 +82,7 @@ int gemv_launch(const GemvPlan &plan, const GemvParams &p, int pro, int epi, cud
 // set kernel attributes (dynamic smem limits) for every variant on the current device;
 // called once per context, outside any stream capture
 int gemv_prepare(void);
+// cuTensorMapEncodeTiled from the driver (nullptr if unavailable)
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();
 
 } // namespace llmrs
