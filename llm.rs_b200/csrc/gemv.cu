@@ -13,27 +13,30 @@
 // into tiles of box_rows (<= 32) rows; a tile is processed in chunks of 32
 // blocks (1024 weights).  One (tile, chunk) pair is one pipeline stage.
 //
-// Data movement.  A producer thread streams each stage with 2-D tensor-map
-// TMA copies straight from the reference's planar layout (row-major nibbles /
-// int8 codes and row-major block scales): four (Q4) or eight (Q8) boxes of
-// rows x 128 bytes with 128-byte swizzle, plus one box of scales.  The swizzle
-// lets lane r read row r's 16-byte block at (r*128 + (chunk ^ (r & 7)) * 16)
-// without bank conflicts.
+// Data movement.  A producer thread streams each stage with two 2-D
+// tensor-map TMA copies straight from the reference's planar layout (a box of
+// rows x 512 bytes of nibbles, or x 1024 bytes of int8 codes, and a box of
+// rows x 32 block scales) into a ring of shared-memory stages.
 //
-// Compute.  Consumer warp w takes stages w, w+4, w+8, ...; lane r of the warp
-// owns row r of the tile and computes that row's 32 block products with dp4a
-// (activation blocks are broadcast reads).  The products are then added to the
-// row's running f32 sum in block order; the running sum is handed from stage
-// to stage through shared memory (an mbarrier chain), so the reference's
-// sequential order holds across chunks while four stages are computed at once.
+// Compute.  16 consumer warps form 4 groups; group g owns tiles g, g+4, ...
+// and ring stages g, g+4, ...  Within a stage, lane l of a warp handles block
+// l for the warp's 8 rows (dp4a products times the two scales); the products
+// are transposed through shared memory so that 4 lanes per row add the 32
+// block products in order (8 each, passed lane to lane).  A row's running sum
+// stays in registers from chunk to chunk, so the reference's sequential order
+// holds while four tiles are computed at once.
 //
-// The producer does not depend on the previous kernel, so with programmatic
-// dependent launch it streams weights while the previous kernel still runs;
-// consumers call griddepcontrol.wait before touching activations.
+// The prologue (RMSNorm where fused, Q8_0 quantisation) runs once per CTA in
+// shared memory.  Activation loads are issued before the weight stream (loads
+// queued behind bulk copies wait for them, L2 hits included).  With
+// programmatic dependent launch the CTA starts while the previous kernel
+// finishes; consumers call griddepcontrol.wait before touching activations.
 #include <cudaTypedefs.h>
 #include <cuda_fp16.h>
 
+#include <cstdlib>
 #include <mutex>
+#include <type_traits>
 
 #include "common.cuh"
 #include "gemv.cuh"
@@ -84,7 +87,7 @@ __host__ __device__ inline SmemLayout smem_layout(int wf, int st, int K, int sta
     L.tb_off = align_up(L.actc_off + (size_t)nb * 4, 16);
     L.link_off = L.tb_off + (size_t)NW * RPW * TBS * 4;
     L.bar_off = align_up(L.link_off + (size_t)NW * RPW * 4, 16);
-    L.red_off = L.bar_off + (size_t)(2 * stages + NW) * 8;
+    L.red_off = L.bar_off + (size_t)(2 * stages + NW + 1) * 8; // full, empty, link, activation-issued
     L.total = align_up(L.red_off + 16 * 4, 16) + 128; // + slack to align the base
     return L;
 }
@@ -148,40 +151,76 @@ __device__ __forceinline__ void load32(const float *src, float (&v)[32])
 // Fill the shared-memory activation (codes, scales, corrections).  One thread
 // per 32-block; `nthr` threads with ids `tid` take part; `bar` is a named
 // barrier id covering exactly those threads.
+// Tell the producer that this warp's activation loads are in flight (one
+// arrival per warp).  Loads issued after a stream of bulk weight copies queue
+// behind it, even when they hit L2, so the producer holds the stream until the
+// activation (a few KB that every CTA needs first) has been requested.
+__device__ __forceinline__ void signal_issued(uint64_t *issued, int tid)
+{
+    if (issued) {
+        __syncwarp();
+        if ((tid & 31) == 0)
+            mbar_arrive(issued);
+    }
+}
+
+template <int WF>
+__device__ __forceinline__ void pack_q8_block(const uint4 c0, const uint4 c1, uint32_t *dst, int *dst_c)
+{
+    const uint32_t in[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+    int q[32], sum = 0;
+#pragma unroll
+    for (int i = 0; i < 32; i++) {
+        q[i] = (int)(int8_t)(in[i >> 2] >> (8 * (i & 3)));
+        sum += q[i];
+    }
+    uint32_t w[8];
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        uint32_t x = 0;
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const int e = WF == 0 ? (j < 4 ? 8 * j + 2 * k : 8 * (j - 4) + 2 * k + 1) : 4 * j + k;
+            x |= (uint32_t)(q[e] & 0xFF) << (8 * k);
+        }
+        w[j] = x;
+    }
+    reinterpret_cast<uint4 *>(dst)[0] = make_uint4(w[0], w[1], w[2], w[3]);
+    reinterpret_cast<uint4 *>(dst)[1] = make_uint4(w[4], w[5], w[6], w[7]);
+    *dst_c = WF == 0 ? -8 * sum : 0;
+}
+
+// Activation prologue: thread t handles blocks t, t + nthr, ...; the first
+// block's loads are issued before signal_issued, later blocks (K > 32 * nthr)
+// load as they go.
 template <int WF, int PRO>
 __device__ void load_activation(const GemvParams &p, uint32_t *act, float *act_s, int *act_c, float *red, int tid,
-                                int nthr, int bar)
+                                int nthr, int bar, uint64_t *issued)
 {
     const int K = p.K, nb = K >> 5;
+    const bool has = tid < nb;
     if (PRO == PRO_Q8) {
-        for (int b = tid; b < nb; b += nthr) {
-            const uint4 c0 = reinterpret_cast<const uint4 *>(p.xq + (size_t)b * 32)[0];
-            const uint4 c1 = reinterpret_cast<const uint4 *>(p.xq + (size_t)b * 32)[1];
-            const uint32_t in[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-            int q[32], sum = 0;
-#pragma unroll
-            for (int i = 0; i < 32; i++) {
-                q[i] = (int)(int8_t)(in[i >> 2] >> (8 * (i & 3)));
-                sum += q[i];
-            }
-            uint32_t w[8];
-#pragma unroll
-            for (int j = 0; j < 8; j++) {
-                uint32_t x = 0;
-#pragma unroll
-                for (int k = 0; k < 4; k++) {
-                    const int e = WF == 0 ? (j < 4 ? 8 * j + 2 * k : 8 * (j - 4) + 2 * k + 1) : 4 * j + k;
-                    x |= (uint32_t)(q[e] & 0xFF) << (8 * k);
-                }
-                w[j] = x;
-            }
-            reinterpret_cast<uint4 *>(act + (size_t)b * 8)[0] = make_uint4(w[0], w[1], w[2], w[3]);
-            reinterpret_cast<uint4 *>(act + (size_t)b * 8)[1] = make_uint4(w[4], w[5], w[6], w[7]);
+        uint4 c0 = make_uint4(0, 0, 0, 0), c1 = c0;
+        float xs = 0.0f;
+        if (has) {
+            c0 = reinterpret_cast<const uint4 *>(p.xq + (size_t)tid * 32)[0];
+            c1 = reinterpret_cast<const uint4 *>(p.xq + (size_t)tid * 32)[1];
+            xs = p.xs[tid];
+        }
+        signal_issued(issued, tid);
+        if (has) {
+            pack_q8_block<WF>(c0, c1, act + (size_t)tid * 8, act_c + tid);
+            act_s[tid] = xs;
+        }
+        for (int b = tid + nthr; b < nb; b += nthr) {
+            const uint4 d0 = reinterpret_cast<const uint4 *>(p.xq + (size_t)b * 32)[0];
+            const uint4 d1 = reinterpret_cast<const uint4 *>(p.xq + (size_t)b * 32)[1];
+            pack_q8_block<WF>(d0, d1, act + (size_t)b * 8, act_c + b);
             act_s[b] = p.xs[b];
-            act_c[b] = WF == 0 ? -8 * sum : 0;
         }
         return;
     }
+    constexpr bool NORM = PRO == PRO_NORM || PRO == PRO_EMBED_NORM;
     const float *x = p.x;
     if (PRO == PRO_EMBED_NORM) {
         int tok = p.state->token;
@@ -191,20 +230,37 @@ __device__ void load_activation(const GemvParams &p, uint32_t *act, float *act_s
             tok = 0;
         }
         x = p.embed + (size_t)tok * K;
-        if (blockIdx.x == 0)
-            for (int i = tid; i < K; i += nthr)
-                p.x_out[i] = x[i];
+    }
+    float v[32], wn[32];
+    if (has) {
+        load32(x + (size_t)tid * 32, v);
+        if (NORM)
+            load32(p.norm_w + (size_t)tid * 32, wn);
+    }
+    signal_issued(issued, tid);
+    if (PRO == PRO_EMBED_NORM && blockIdx.x == 0) { // the residual stream starts as the embedding row
+        if (has)
+#pragma unroll
+            for (int i = 0; i < 32; i++)
+                p.x_out[(size_t)tid * 32 + i] = v[i];
+        for (int b = tid + nthr; b < nb; b += nthr)
+            for (int i = 0; i < 32; i++)
+                p.x_out[(size_t)b * 32 + i] = x[(size_t)b * 32 + i];
     }
     float scale = 1.0f;
-    if (PRO == PRO_NORM || PRO == PRO_EMBED_NORM) {
+    if (NORM) {
         // sum of squares in a fixed order (per thread, then a fixed tree)
         float ss = 0.0f;
-        for (int b = tid; b < nb; b += nthr) {
-            float v[32];
-            load32(x + (size_t)b * 32, v);
+        if (has)
 #pragma unroll
             for (int i = 0; i < 32; i++)
                 ss = __fadd_rn(ss, __fmul_rn(v[i], v[i]));
+        for (int b = tid + nthr; b < nb; b += nthr) {
+            float u[32];
+            load32(x + (size_t)b * 32, u);
+#pragma unroll
+            for (int i = 0; i < 32; i++)
+                ss = __fadd_rn(ss, __fmul_rn(u[i], u[i]));
         }
         ss = warp_sum(ss);
         const int warp = tid >> 5;
@@ -217,17 +273,24 @@ __device__ void load_activation(const GemvParams &p, uint32_t *act, float *act_s
         const float rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)K), p.eps));
         scale = __fdiv_rn(1.0f, rms);
     }
-    for (int b = tid; b < nb; b += nthr) {
-        float v[32];
-        load32(x + (size_t)b * 32, v);
-        if (PRO == PRO_NORM || PRO == PRO_EMBED_NORM) {
-            float wn[32];
-            load32(p.norm_w + (size_t)b * 32, wn);
+    if (has) {
+        if (NORM)
 #pragma unroll
             for (int i = 0; i < 32; i++)
                 v[i] = __fmul_rn(__fmul_rn(v[i], scale), wn[i]);
+        quantize_pack<WF>(v, act + (size_t)tid * 8, act_s + tid, act_c + tid);
+    }
+    for (int b = tid + nthr; b < nb; b += nthr) {
+        float u[32];
+        load32(x + (size_t)b * 32, u);
+        if (NORM) {
+            float un[32];
+            load32(p.norm_w + (size_t)b * 32, un);
+#pragma unroll
+            for (int i = 0; i < 32; i++)
+                u[i] = __fmul_rn(__fmul_rn(u[i], scale), un[i]);
         }
-        quantize_pack<WF>(v, act + (size_t)b * 8, act_s + b, act_c + b);
+        quantize_pack<WF>(u, act + (size_t)b * 8, act_s + b, act_c + b);
     }
 }
 
@@ -341,18 +404,32 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     float *linkbuf = reinterpret_cast<float *>(smem + L.link_off);
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + L.bar_off);
     uint64_t *empty = full + S;
-    uint64_t *link = empty + S; // link[w]: warp w hands its rows' running sums to the next group
+    uint64_t *link = empty + S;   // link[w]: warp w hands its rows' running sums on
+    uint64_t *issued = link + NW; // every consumer warp has requested its activation
     float *red = reinterpret_cast<float *>(smem + L.red_off);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    // A stage is owned by one warp group at a time; with more active groups
-    // than stages minus one, a parity wait on a stage barrier could alias a phase.
-    const int nga = max(1, min(NG, S - 1));
+    // TPS tile sets are worked on at once (4 when the CTA has >= 4 tiles, else
+    // 2 or 1); the GT = NG / TPS groups of a set take its (tile, chunk) steps
+    // u = 0, 1, ... in turn, group q of the set taking u = q, q + GT, ...  With
+    // GT = 1 a row's running sum stays in registers; with GT > 1 it is handed
+    // from group to group through shared memory (one mbarrier per warp), which
+    // keeps the reference's block order while GT chunks are computed at once.
+    // Group g also owns ring stages g, g + NG, ...: a stage barrier is only
+    // awaited by the group that consumed its previous phase.
+    const int SPG = S / NG; // stages per group
     const int B = p.box_rows;
     const int r0 = blockIdx.x * p.rows_per_cta;
     const int r1 = min(p.N, r0 + p.rows_per_cta);
     const int ntiles = (r1 - r0 + B - 1) / B;
-    const int iters = ntiles * nchunks;
+    const int TPS_rt = ntiles >= NG ? NG : (ntiles >= 2 ? 2 : 1);
+    const int GT_rt = NG / TPS_rt;
+    auto group_iters = [&](int g) {
+        const int set = g % TPS_rt, q = g / TPS_rt;
+        const int nset = ntiles > set ? (ntiles - 1 - set) / TPS_rt + 1 : 0;
+        const int U = nset * nchunks;
+        return U > q ? (U - 1 - q) / GT_rt + 1 : 0;
+    };
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; s++) {
@@ -361,6 +438,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         }
         for (int w = 0; w < NW; w++)
             mbar_init(&link[w], 1);
+        mbar_init(issued, NW);
         fence_mbar_init();
         trace_start(p.trace, p.trace_slot);
     }
@@ -368,22 +446,52 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 
     if (warp == NW) {
         // ------------------------------------------------------------ producer
-        // weights do not depend on the previous kernel: stream them right away
+        // Weights do not depend on the previous kernel: the first n_pre stages
+        // stream right away, the rest once the consumers have requested the
+        // activation (queued behind the weight stream it would arrive last).
         if (lane == 0) {
             const uint64_t pol = policy_evict_first();
             const uint32_t stage_tx = (uint32_t)(B * (W_ROW + S_ROW)); // whole boxes (OOB is zero-filled)
-            for (int it = 0; it < iters; it++) {
-                const int s = it % S;
-                LLMRS_TRACE_BEGIN(0);
-                if (it >= S && !mbar_wait(&empty[s], ((it / S) - 1) & 1, p.err))
-                    return;
-                LLMRS_TRACE_END(0);
-                const int tile = it / nchunks, c = it % nchunks;
-                const int y = r0 + tile * B;
-                uint8_t *st = smem + (size_t)s * L.stage_bytes;
-                mbar_arrive_expect_tx(&full[s], stage_tx);
-                tma_load_2d(st, &tw, c * (W_ROW / 4), y, &full[s], pol);
-                tma_load_2d(st + L.scale_off, &ts, c * CB, y, &full[s], pol);
+            const int pre = min(p.n_pre, S);
+            // One thread issues every stage, so its loop is kept free of
+            // divisions: per group, the step's chunk and tile advance by GT.
+            int gi[NG], gc[NG], gt[NG];
+#pragma unroll
+            for (int g = 0; g < NG; g++) {
+                gi[g] = group_iters(g);
+                gc[g] = g / TPS_rt; // first step u = q: chunk u % nchunks of tile set g % TPS_rt
+                gt[g] = g % TPS_rt;
+                while (gc[g] >= nchunks) {
+                    gc[g] -= nchunks;
+                    gt[g] += TPS_rt;
+                }
+            }
+            const int spg_shift = SPG == 2 ? 1 : 0; // stages are 4 or 8: SPG is 1 or 2
+            int issued_n = 0;
+            for (int k = 0; k < gi[0]; k++) { // group 0 has the most steps
+                const int slot = k & (SPG - 1), use = k >> spg_shift;
+#pragma unroll
+                for (int g = 0; g < NG; g++) {
+                    if (k >= gi[g])
+                        continue;
+                    if (issued_n++ == pre && !mbar_wait(issued, 0, p.err))
+                        return;
+                    const int s = g + NG * slot;
+                    LLMRS_TRACE_BEGIN(0);
+                    if (use > 0 && !mbar_wait(&empty[s], (use - 1) & 1, p.err))
+                        return;
+                    LLMRS_TRACE_END(0);
+                    const int y = r0 + gt[g] * B, c = gc[g];
+                    uint8_t *st = smem + (size_t)s * L.stage_bytes;
+                    mbar_arrive_expect_tx(&full[s], stage_tx);
+                    tma_load_2d(st, &tw, c * (W_ROW / 4), y, &full[s], pol);
+                    tma_load_2d(st + L.scale_off, &ts, c * CB, y, &full[s], pol);
+                    gc[g] += GT_rt;
+                    while (gc[g] >= nchunks) {
+                        gc[g] -= nchunks;
+                        gt[g] += TPS_rt;
+                    }
+                }
             }
             LLMRS_TRACE_FLUSH(1);
         }
@@ -398,27 +506,47 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     const int ctid = threadIdx.x;
     if (ctid == 0)
         trace_go(p.trace, p.trace_slot);
-    load_activation<WF, PRO>(p, act, act_s, act_c, red, ctid, PRO_THREADS, 1);
+    load_activation<WF, PRO>(p, act, act_s, act_c, red, ctid, PRO_THREADS, 1, issued);
     named_bar_sync(1, PRO_THREADS);
     LLMRS_TRACE_END(2);
 
-    // warp (grp, wq): group grp = warp / WPG takes stages it = grp, grp+nga, ...;
-    // wq = warp % WPG takes tile rows wq*RPW .. +RPW-1.  Lane l = block l of the chunk.
+    // warp (grp, wq): group grp = warp / WPG takes every chunk of tiles grp,
+    // grp + NG, ...; wq = warp % WPG takes tile rows wq*RPW .. +RPW-1.  Lane l =
+    // block l of the chunk.
     const int grp = warp / WPG, wq = warp % WPG;
-    const int prevw = ((grp + nga - 1) % nga) * WPG + wq;
     float *tb = tbuf + (size_t)warp * RPW * TBS;
     // transposed roles: lane j sums row ri = j % RPW over blocks seg*8 .. seg*8+7
     const int ri = lane % RPW, seg = lane / RPW;
     unsigned long long best = 0ull;
     bool ok = true;
-    for (int it = grp; grp < nga && it < iters; it += nga) {
-        const int s = it % S;
-        const int tile = it / nchunks, c = it % nchunks;
+    // the step loop, specialised for the number of groups per tile set
+    auto steps = [&](auto gt_tag) {
+    constexpr int GT = decltype(gt_tag)::value;
+    constexpr int TPS = NG / GT;
+    float acc = 0.0f; // running sum of row ri (complete in the segment-3 lanes)
+    const int tset = grp % TPS, q = grp / TPS;
+    const int prevw = (tset + TPS * ((q + GT - 1) % GT)) * WPG + wq; // previous step's warp
+    const int my_iters = group_iters(grp);
+    int c = q, tile = tset; // this group's first step u = q
+    while (c >= nchunks) {
+        c -= nchunks;
+        tile += TPS;
+    }
+    for (int k = 0; k < my_iters; k++) {
+        if (k > 0) { // next step: u += GT
+            c += GT;
+            while (c >= nchunks) {
+                c -= nchunks;
+                tile += TPS;
+            }
+        }
+        const int s = grp + NG * (k & (SPG - 1));
+        const int u = k * GT + q;
         const int trow0 = r0 + tile * B;
         const int rows = min(B, r1 - trow0);
         const int nbc = min(CB, nb - c * CB);
         LLMRS_TRACE_BEGIN(3);
-        if (ok && !mbar_wait(&full[s], (it / S) & 1, p.err))
+        if (ok && !mbar_wait(&full[s], (uint32_t)((SPG == 2 ? k >> 1 : k) & 1), p.err))
             ok = false;
         LLMRS_TRACE_END(3);
         LLMRS_TRACE_BEGIN(4);
@@ -458,13 +586,18 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         const float4 v0 = *reinterpret_cast<const float4 *>(tb + ri * TBS + seg * 8);
         const float4 v1 = *reinterpret_cast<const float4 *>(tb + ri * TBS + seg * 8 + 4);
         const float v[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
-        // running sum of row ri from the previous stage (same rows, previous group)
-        float acc = 0.0f;
-        if (it > 0) {
-            if (ok && !mbar_wait(&link[prevw], ((it - 1) / nga) & 1, p.err))
-                ok = false;
-            if (c > 0 && seg == 0)
-                acc = linkbuf[prevw * RPW + ri];
+        if (GT == 1) { // the running sum moves from the segment-3 lane to the segment-0 lane
+            const float carry = __shfl_sync(0xffffffffu, acc, 3 * RPW + ri);
+            acc = (c > 0 && seg == 0) ? carry : 0.0f;
+        } else { // ... or arrives from the previous step's warp
+            acc = 0.0f;
+            if (u > 0) {
+                const int kp = q > 0 ? k : k - 1; // that warp's step index
+                if (ok && !mbar_wait(&link[prevw], (uint32_t)(kp & 1), p.err))
+                    ok = false;
+                if (c > 0 && seg == 0)
+                    acc = linkbuf[prevw * RPW + ri];
+            }
         }
         // add the chunk's blocks in order: segment 0 first, then 1, 2, 3
         const bool live_row = wq * RPW + ri < rows;
@@ -482,12 +615,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                         acc = __fadd_rn(acc, v[k]);
             }
         }
-        __syncwarp();
-        if (seg == 3)
-            linkbuf[warp * RPW + ri] = acc;
-        __syncwarp();
-        if (lane == 0)
-            mbar_arrive(&link[warp]);
+        if (GT > 1) {
+            __syncwarp();
+            if (seg == 3)
+                linkbuf[warp * RPW + ri] = acc;
+            __syncwarp();
+            if (lane == 0)
+                mbar_arrive(&link[warp]);
+        }
         LLMRS_TRACE_END(4);
         if (c == nchunks - 1) {
             // ---- epilogue: lanes of segment 3 hold the complete rows
@@ -515,6 +650,13 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             }
         }
     }
+    };
+    if (GT_rt == 1)
+        steps(std::integral_constant<int, 1>{});
+    else if (GT_rt == 2)
+        steps(std::integral_constant<int, 2>{});
+    else
+        steps(std::integral_constant<int, 4>{});
     if (EPI == EPI_ARGMAX)
         argmax_finalize(p, best, ctid, PRO_THREADS, 1);
     LLMRS_TRACE_FLUSH(0);
@@ -537,7 +679,7 @@ __global__ void __launch_bounds__(SIMPLE_THREADS) gemv_simple_kernel(const GemvP
     int *act_c = reinterpret_cast<int *>(act_s + nb);
     float *red = reinterpret_cast<float *>(act_c + nb);
     griddep_wait();
-    load_activation<WF, PRO>(p, act, act_s, act_c, red, threadIdx.x, SIMPLE_THREADS, 1);
+    load_activation<WF, PRO>(p, act, act_s, act_c, red, threadIdx.x, SIMPLE_THREADS, 1, nullptr);
     named_bar_sync(1, SIMPLE_THREADS);
     const int row = blockIdx.x * blockDim.x + threadIdx.x;
     unsigned long long best = 0ull;
@@ -616,6 +758,7 @@ int launch_one(const GemvPlan &plan, const GemvParams &p0, cudaStream_t stream, 
     GemvParams p = p0;
     if (plan.fast) {
         p.n_stages = plan.stages;
+        p.n_pre = gemv_prefetch_stages();
         p.box_rows = plan.box_rows;
         p.rows_per_cta = plan.rows_per_cta;
         LLMRS_CUDA_TRY(launch(gemv_tma_kernel<WF, ST, PRO, EPI>, dim3(plan.grid), dim3(NTHREADS), plan.smem, stream,
@@ -673,7 +816,7 @@ int encode_2d(CUtensorMap *map, const void *base, int elem, size_t row_bytes, in
 static size_t smem_bytes_for(int wf, int st, int K, int *stages)
 {
     int best = 0;
-    for (int s = MAX_STAGES; s >= 2; s--) {
+    for (int s = MAX_STAGES; s >= NG; s -= NG) { // each warp group owns stages/NG of them
         if (smem_layout(wf, st, K, s).total <= SMEM_BUDGET) {
             best = s;
             break;
@@ -746,6 +889,16 @@ int gemv_launch(const GemvPlan &plan, const GemvParams &p, int pro, int epi, cud
     LLMRS_GEMV_VARIANTS(LLMRS_GEMV_CASE)
 #undef LLMRS_GEMV_CASE
     return fail(LLMRS_ENOTSUP, "gemv: unsupported variant wf=%d st=%d pro=%d epi=%d", wf, st, pro, epi);
+}
+
+int gemv_prefetch_stages(void)
+{
+    static const int n = [] {
+        const char *e = getenv("LLMRS_GEMV_PREFETCH");
+        const int v = e ? atoi(e) : 0;
+        return v < 0 ? 0 : v;
+    }();
+    return n;
 }
 
 int gemv_prepare(void)

@@ -55,6 +55,7 @@ struct GemvParams {
     int *token_log;        // EPI_ARGMAX: appended greedy tokens
     uint32_t *err;         // device error word
     int n_stages;          // set by gemv_launch from the plan
+    int n_pre;             // stages streamed before the activation is requested (set by gemv_launch)
     int box_rows;
     int rows_per_cta;
     unsigned long long *trace; // optional timeline marks, 3 per kernel (see trace_start)
@@ -82,6 +83,9 @@ int gemv_launch(const GemvPlan &plan, const GemvParams &p, int pro, int epi, cud
 // set kernel attributes (dynamic smem limits) for every variant on the current device;
 // called once per context, outside any stream capture
 int gemv_prepare(void);
+// weight stages a GEMV streams before its activation loads are issued
+// (LLMRS_GEMV_PREFETCH, default 0)
+int gemv_prefetch_stages(void);
 // cuTensorMapEncodeTiled from the driver (nullptr if unavailable)
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();
 
