@@ -25,7 +25,7 @@ sys.path.insert(0, ROOT)
 
 WORKLOADS = {
     "8b": dict(cfg=dict(n_layers=32, hidden=4096, n_heads=32, n_kv_heads=8, head_dim=128, ffn=14336,
-                        vocab=128256, max_seq=4352, rms_eps=1e-5, rope_theta=500000.0, weight_format=0,
+                        vocab=128256, max_seq=4608, rms_eps=1e-5, rope_theta=500000.0, weight_format=0,
                         tied_embeddings=0),
                kv=4096, name="llama3-8b-shaped Q4_0 decode, KV pre-filled to 4096 (config 3)"),
     "1b": dict(cfg=dict(n_layers=16, hidden=2048, n_heads=32, n_kv_heads=8, head_dim=64, ffn=8192,
@@ -38,6 +38,12 @@ WORKLOADS = {
                 kv=2048, name="llama3-70b-shaped Q4_0 decode, KV pre-filled to 2048 (config 5)"),
 }
 SEED = 0x5EED
+
+# DRAM bytes per launch of each decode-step GEMV of the 8B shape, from one ncu
+# capture (dram__bytes_read.sum + dram__bytes_write.sum; profiles/
+# decode_step_8b_kv4096_launches.md has the command and the table).
+MEASURED_GEMV_DRAM_8B = {"qkv_gemv": 14.27e6, "o_gemv": 9.54e6, "gate_up_gemv": 66.18e6, "down_gemv": 33.18e6,
+                         "lm_head_gemv": 296.07e6}
 
 
 def load_peaks():
@@ -111,10 +117,15 @@ class ClockSampler:
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
         try:
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.device), "--query-gpu=" + q,
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
+            # start timing only once the sampler is producing (startup takes ~0.1-1 s)
+            t_end = time.time() + 5.0
+            while not self.lines and time.time() < t_end:
+                time.sleep(0.01)
+            self.lines.clear()
         except Exception:
             self.proc = None
         return self
@@ -181,6 +192,8 @@ def run_ours(args, rank, world):
     local = int(os.environ.get("LOCAL_RANK", "0"))
     wl = WORKLOADS[args.workload]
     c = dict(wl["cfg"])
+    if args.layers:
+        c["n_layers"] = args.layers
     ctx = L.Context(local)
     m = L.Model(ctx, c)
     m.init_synthetic(SEED)
@@ -221,6 +234,9 @@ def run_ours(args, rank, world):
     gemv_bytes_step = sum(gemv_bytes(k, c) * kind_count[k] for k in gemv_kinds)
     gemv_ms_step = sum(kind_ms[k] for k in gemv_kinds)
     gemv_launches = sum(kind_count[k] for k in gemv_kinds)
+    traffic = None
+    if args.workload == "8b" and not args.layers:
+        traffic = round(sum(MEASURED_GEMV_DRAM_8B[k] * kind_count[k] for k in gemv_kinds) / gemv_launches)
     peak, peak_src = load_peaks()
     achieved = gemv_bytes_step / (gemv_ms_step / 1000.0) / 1e9
     S_mid = kv0 + K // 2
@@ -256,7 +272,8 @@ def run_ours(args, rank, world):
                                                                                               kv_bytes / 1e9)},
         "roofline": {"bound": "hbm", "kernel": "gemv_tma_kernel (all Q4 GEMVs of one decode step)",
                      "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                     "frac": round(achieved / peak, 4), "traffic": None, "peak_source": peak_src,
+                     "frac": round(achieved / peak, 4), "traffic": traffic, "traffic_unit": "bytes per launch",
+                     "algorithmic_bytes_per_launch": round(gemv_bytes_step / gemv_launches), "peak_source": peak_src,
                      "gemv_launches_per_step": gemv_launches, "gemv_bytes_per_step": gemv_bytes_step,
                      "per_kernel_ms": {k: round(v, 4) for k, v in kind_ms.items()},
                      "step_algorithmic_bytes": tot_bytes, "step_achieved_gbs": round(step_gbs, 1),
@@ -303,11 +320,13 @@ def run_reference(args, rank, world):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=64)
+    ap.add_argument("--steps", type=int, default=256)
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="8b")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--layers", type=int, default=0,
+                    help="override the layer count (small cases for ncu captures; not a bench line)")
     args = ap.parse_args()
     assert args.warmup >= 3, "at least 3 warm-up steps"
     world = int(os.environ.get("WORLD_SIZE", "1"))

@@ -225,8 +225,9 @@ int llmrs_model_decode_kernel_count(llmrs_model *model, int *count);
 int llmrs_model_profile_decode(llmrs_model *model, int token, int pos, float *ms_out, int *kind_out, int *n);
 /* run one decode step through a traced copy of the step graph (same launches,
  * same programmatic overlap) and return a device timeline: for kernel i,
- * h_marks[3i] = first CTA start, [3i+1] = first CTA past its wait on the previous
- * kernel, [3i+2] = last CTA end (globaltimer ns); kinds[i] as in profile_decode.
+ * h_marks[4i] = first CTA start, [4i+1] = first CTA past its wait on the previous
+ * kernel, [4i+2] = last CTA done with its activation prologue, [4i+3] = last CTA
+ * end (globaltimer ns); kinds[i] as in profile_decode.
  * *n: in = capacity (kernels), out = kernels of the step */
 int llmrs_model_trace_decode(llmrs_model *model, int token, int pos, unsigned long long *h_marks, int *kinds, int *n);
 /* time `iters` device-resident decode steps (graph replays) with CUDA events

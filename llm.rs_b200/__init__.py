@@ -451,15 +451,17 @@ class Model:
 
     def trace_decode(self, token, pos):
         """Device timeline of one graph-launched decode step: list of
-        (kind, start_ns, go_ns, end_ns) relative to the first kernel's start."""
+        (kind, start_ns, go_ns, ready_ns, end_ns) relative to the first kernel's
+        start (ready: last CTA done with its activation prologue)."""
         cap = self.decode_kernel_count()
-        marks = np.zeros(3 * cap, np.uint64)
+        marks = np.zeros(4 * cap, np.uint64)
         kinds = np.zeros(cap, np.int32)
         n = ctypes.c_int(cap)
         check(lib().llmrs_model_trace_decode(self.h, int(token), int(pos), _ptr(marks), _ptr(kinds), ctypes.byref(n)))
-        marks = marks[:3 * n.value].reshape(-1, 3).astype(np.int64)
+        marks = marks[:4 * n.value].reshape(-1, 4).astype(np.int64)
         t0 = int(marks[0, 0])
-        return [(self.KERNEL_KINDS[k], int(a - t0), int(b - t0), int(c - t0)) for k, (a, b, c) in zip(kinds, marks)]
+        return [(self.KERNEL_KINDS[k], int(a - t0), int(b - t0), int(r - t0), int(c - t0))
+                for k, (a, b, r, c) in zip(kinds, marks)]
 
     def time_decode(self, token, pos, iters):
         ms = ctypes.c_float(0)

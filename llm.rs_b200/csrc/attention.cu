@@ -25,6 +25,7 @@
 
 #include "attention.cuh"
 #include "common.cuh"
+#include "prefetch.cuh"
 
 namespace llmrs {
 
@@ -248,6 +249,8 @@ __global__ void __launch_bounds__(AttnWarps<D>::value * 32, 1) attn_decode_kerne
         const uint64_t pol = policy_evict_first();
         for (int j = 0; j < 2 && j < mine; j++)
             issue(j, pol);
+        if (warp == NW - 1)
+            issue_next_prefetch(p.pf, blockIdx.y * gridDim.x + blockIdx.x, gridDim.x * gridDim.y);
     }
     __syncwarp();
     if (warp < NREP) { // RoPE(q) of head `warp` into shared memory
@@ -268,6 +271,8 @@ __global__ void __launch_bounds__(AttnWarps<D>::value * 32, 1) attn_decode_kerne
     }
     __syncthreads(); // q_s complete
     LLMRS_ATTN_MARK(1);
+    if (threadIdx.x == 0)
+        trace_ready(p.trace, p.trace_slot);
 
     float m_run = -INFINITY, l_run = 0.0f; // softmax state of head lane % NREP
     float acc[NREP][DL];

@@ -109,6 +109,24 @@ __device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, i
         : "memory");
 }
 
+// bulk prefetch of [p, p + bytes) into L2 (16-byte aligned, multiple of 16)
+__device__ __forceinline__ void prefetch_l2(const void *p, uint32_t bytes)
+{
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+// prefetch an arbitrary byte range, rounded inward to 16-byte units, in
+// pieces of at most 64 KB
+__device__ __forceinline__ void prefetch_l2_range(const uint8_t *p, size_t bytes)
+{
+    const uintptr_t a0 = ((uintptr_t)p + 15) & ~(uintptr_t)15;
+    const uintptr_t a1 = ((uintptr_t)p + bytes) & ~(uintptr_t)15;
+    for (uintptr_t a = a0; a < a1; a += 65536) {
+        const uintptr_t n = a1 - a < 65536 ? a1 - a : 65536;
+        prefetch_l2(reinterpret_cast<const void *>(a), (uint32_t)n);
+    }
+}
+
 // order this thread's earlier generic-proxy shared-memory accesses before its
 // later async-proxy (bulk copy) accesses of the same bytes
 __device__ __forceinline__ void fence_proxy_async_smem()
@@ -197,25 +215,34 @@ __device__ __forceinline__ void named_bar_sync(int id, int nthreads)
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
-// Timeline marks of a traced decode step (globaltimer ns), three per kernel:
-// [3*slot] first CTA start, [3*slot+1] first CTA past griddepcontrol.wait,
-// [3*slot+2] last CTA end.
+// Timeline marks of a traced decode step (globaltimer ns), four per kernel:
+// [4*slot] first CTA start, [4*slot+1] first CTA past griddepcontrol.wait,
+// [4*slot+2] last CTA ready to consume its stream (activation prologue done),
+// [4*slot+3] last CTA end.
+constexpr int TRACE_MARKS = 4;
+
 __device__ __forceinline__ void trace_start(unsigned long long *trace, int slot)
 {
     if (trace)
-        atomicMin(&trace[3 * slot], (unsigned long long)globaltimer_ns());
+        atomicMin(&trace[TRACE_MARKS * slot], (unsigned long long)globaltimer_ns());
 }
 
 __device__ __forceinline__ void trace_go(unsigned long long *trace, int slot)
 {
     if (trace)
-        atomicMin(&trace[3 * slot + 1], (unsigned long long)globaltimer_ns());
+        atomicMin(&trace[TRACE_MARKS * slot + 1], (unsigned long long)globaltimer_ns());
+}
+
+__device__ __forceinline__ void trace_ready(unsigned long long *trace, int slot)
+{
+    if (trace)
+        atomicMax(&trace[TRACE_MARKS * slot + 2], (unsigned long long)globaltimer_ns());
 }
 
 __device__ __forceinline__ void trace_end(unsigned long long *trace, int slot)
 {
     if (trace)
-        atomicMax(&trace[3 * slot + 2], (unsigned long long)globaltimer_ns());
+        atomicMax(&trace[TRACE_MARKS * slot + 3], (unsigned long long)globaltimer_ns());
 }
 
 // order-preserving key for a float + lowest-index tie break (max of keys = argmax)

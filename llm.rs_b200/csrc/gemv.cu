@@ -40,6 +40,7 @@
 
 #include "common.cuh"
 #include "gemv.cuh"
+#include "prefetch.cuh"
 
 // Optional phase tracing (cycle counters around pipeline waits); compiled out
 // unless a tracing build defines LLMRS_GEMV_TRACE and provides the hooks.
@@ -493,6 +494,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     }
                 }
             }
+            issue_next_prefetch(p.pf, blockIdx.x, gridDim.x);
             LLMRS_TRACE_FLUSH(1);
         }
         return;
@@ -508,6 +510,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         trace_go(p.trace, p.trace_slot);
     load_activation<WF, PRO>(p, act, act_s, act_c, red, ctid, PRO_THREADS, 1, issued);
     named_bar_sync(1, PRO_THREADS);
+    if (ctid == 0)
+        trace_ready(p.trace, p.trace_slot);
     LLMRS_TRACE_END(2);
 
     // warp (grp, wq): group grp = warp / WPG takes every chunk of tiles grp,

@@ -35,6 +35,27 @@ struct StepState {
     int pad;
 };
 
+// What the next kernel of a decode step reads first, prefetched into L2 by the
+// current kernel once its own stream is requested: the HBM keeps streaming
+// through the current kernel's tail, the launch gap and the next prologue.
+enum NextPrefetchKind : int {
+    PF_NONE = 0,
+    PF_ROWS = 1, // next is a GEMV: CTA j -> [a + j*a_stride, +a_bytes) and [b + j*b_stride, +b_bytes)
+    PF_KV = 2,   // next is decode attention: CTA j -> split j % n_splits of KV head j / n_splits
+};
+
+struct NextPrefetch {
+    int kind = PF_NONE;
+    int ncta = 0;                      // CTAs of the next kernel that get a range
+    const uint8_t *a = nullptr, *b = nullptr;
+    size_t a_stride = 0, a_bytes = 0, a_end = 0; // a_end, b_end: bytes of the whole tensor
+    size_t b_stride = 0, b_bytes = 0, b_end = 0;
+    const float *kc = nullptr, *vc = nullptr;    // PF_KV
+    const StepState *state = nullptr;            // PF_KV: decode position
+    int max_seq = 0, head_dim = 0, n_splits = 0;
+    size_t kv_bytes = 0;               // PF_KV: cap per K or V range
+};
+
 struct GemvParams {
     const uint8_t *w;      // Q4: [N][K/2] nibbles; Q8: [N][K] codes
     const void *scales;    // [N][K/32] f16 or f32
@@ -60,6 +81,7 @@ struct GemvParams {
     int rows_per_cta;
     unsigned long long *trace; // optional timeline marks, 3 per kernel (see trace_start)
     int trace_slot;
+    NextPrefetch pf;       // the next kernel's first bytes (PF_NONE: nothing)
 };
 
 // Launch geometry + TMA descriptors of one weight matrix, built once per weight.

@@ -142,7 +142,7 @@ struct llmrs_model {
     // graph of one decode step (and a copy that records a device timeline)
     cudaGraphExec_t graph = nullptr;
     cudaGraphExec_t graph_traced = nullptr;
-    unsigned long long *d_trace = nullptr; // 3 marks per kernel
+    unsigned long long *d_trace = nullptr; // TRACE_MARKS marks per kernel
     // pinned host staging
     int *h_stage = nullptr; // 13 slots of 4 ints (token, pos) for H2D; [60..61]: next token, err
     int h_stage_n = 0;
@@ -587,7 +587,7 @@ int llmrs_model_create(llmrs_ctx *ctx, const llmrs_config *cfg, llmrs_model **ou
     m->att_counter = (unsigned int *)A.take((size_t)m->Hkv * 4);
     m->state = (StepState *)A.take(sizeof(StepState));
     m->token_log = (int *)A.take((size_t)m->log_cap * 4);
-    m->d_trace = (unsigned long long *)A.take((size_t)3 * (5 * cfg->n_layers + 8) * 8);
+    m->d_trace = (unsigned long long *)A.take((size_t)TRACE_MARKS * (5 * cfg->n_layers + 8) * 8);
     if (!m->token_log || !m->d_trace) {
         model_free(m);
         return fail(LLMRS_ENOMEM, "model arena layout overflow");
@@ -839,6 +839,64 @@ struct KernelTimer {
     }
 };
 
+// Bytes per CTA that a decode-step kernel prefetches into L2 for the next
+// kernel (LLMRS_L2_PREFETCH_KB; default 0 = off: on B200 the next kernel's
+// latency is set by its dependency wait and prologue, not by its first HBM
+// bytes, so the prefetch only adds traffic).
+static size_t l2_prefetch_cap(void)
+{
+    static const size_t cap = [] {
+        const char *e = getenv("LLMRS_L2_PREFETCH_KB");
+        const long v = e ? atol(e) : 0;
+        return (size_t)(v < 0 ? 0 : v) * 1024;
+    }();
+    return cap;
+}
+
+// next kernel is the GEMV over q: each of its CTAs gets its first rows
+static NextPrefetch prefetch_rows(const QW &q)
+{
+    NextPrefetch pf;
+    const size_t cap = l2_prefetch_cap();
+    if (!q.plan.fast || cap == 0)
+        return pf;
+    const size_t wrow = q.plan.wf == 0 ? (size_t)q.k / 2 : (size_t)q.k;
+    const size_t srow = (size_t)(q.k / 32) * (q.plan.st == LLMRS_F16 ? 2 : 4);
+    const size_t rpc = (size_t)q.plan.rows_per_cta;
+    size_t rows = cap / (wrow + srow);
+    rows = rows < rpc ? rows : rpc;
+    pf.kind = PF_ROWS;
+    pf.ncta = q.plan.grid;
+    pf.a = q.w;
+    pf.a_stride = rpc * wrow;
+    pf.a_bytes = rows * wrow;
+    pf.a_end = (size_t)q.n * wrow;
+    pf.b = reinterpret_cast<const uint8_t *>(q.s);
+    pf.b_stride = rpc * srow;
+    pf.b_bytes = rows * srow;
+    pf.b_end = (size_t)q.n * srow;
+    return pf;
+}
+
+// next kernel is decode attention over layer L's cache
+static NextPrefetch prefetch_kv(const llmrs_model *m, const LayerW &L)
+{
+    NextPrefetch pf;
+    const size_t cap = l2_prefetch_cap();
+    if (cap == 0)
+        return pf;
+    pf.kind = PF_KV;
+    pf.ncta = m->n_splits * m->Hkv;
+    pf.kc = L.kc;
+    pf.vc = L.vc;
+    pf.state = m->state;
+    pf.max_seq = m->S;
+    pf.head_dim = m->D;
+    pf.n_splits = m->n_splits;
+    pf.kv_bytes = cap / 2;
+    return pf;
+}
+
 static int enqueue_step(llmrs_model *m, cudaStream_t s, KernelTimer *kt = nullptr, unsigned long long *trace = nullptr)
 {
     int slot = 0;
@@ -872,6 +930,7 @@ static int enqueue_step(llmrs_model *m, cudaStream_t s, KernelTimer *kt = nullpt
             p.vocab = m->V;
             p.x_out = m->x;
         }
+        p.pf = prefetch_kv(m, L);
         LLMRS_TRY(mark(0));
         LLMRS_TRY(gemv_launch(L.qkv.plan, p, pro, EPI_STORE, s, overlap && l != 0));
         LLMRS_TRY(mark(-1));
@@ -895,6 +954,7 @@ static int enqueue_step(llmrs_model *m, cudaStream_t s, KernelTimer *kt = nullpt
         a.inv_sqrt_d = 1.0f / sqrtf((float)m->D);
         a.trace = trace;
         a.trace_slot = slot++;
+        a.pf = prefetch_rows(L.o);
         LLMRS_TRY(mark(1));
         LLMRS_TRY(attention_decode_launch(a, s, overlap));
         LLMRS_TRY(mark(-1));
@@ -910,6 +970,7 @@ static int enqueue_step(llmrs_model *m, cudaStream_t s, KernelTimer *kt = nullpt
         o.residual = m->x;
         o.trace = trace;
         o.trace_slot = slot++;
+        o.pf = prefetch_rows(L.gate_up);
         LLMRS_TRY(mark(2));
         LLMRS_TRY(gemv_launch(L.o.plan, o, PRO_F32, EPI_RESIDUAL, s, overlap));
         LLMRS_TRY(mark(-1));
@@ -926,6 +987,7 @@ static int enqueue_step(llmrs_model *m, cudaStream_t s, KernelTimer *kt = nullpt
         g.y = m->act;
         g.trace = trace;
         g.trace_slot = slot++;
+        g.pf = prefetch_rows(L.down);
         LLMRS_TRY(mark(3));
         LLMRS_TRY(gemv_launch(L.gate_up.plan, g, PRO_NORM, EPI_SILU, s, overlap));
         LLMRS_TRY(mark(-1));
@@ -941,6 +1003,7 @@ static int enqueue_step(llmrs_model *m, cudaStream_t s, KernelTimer *kt = nullpt
         d.residual = m->x;
         d.trace = trace;
         d.trace_slot = slot++;
+        d.pf = l + 1 < m->cfg.n_layers ? prefetch_rows(m->layers[l + 1].qkv) : prefetch_rows(m->lm_head);
         LLMRS_TRY(mark(4));
         LLMRS_TRY(gemv_launch(L.down.plan, d, PRO_F32, EPI_RESIDUAL, s, overlap));
         LLMRS_TRY(mark(-1));
@@ -960,6 +1023,7 @@ static int enqueue_step(llmrs_model *m, cudaStream_t s, KernelTimer *kt = nullpt
     h.token_log = m->token_log;
     h.trace = trace;
     h.trace_slot = slot++;
+    h.pf = prefetch_rows(m->layers[0].qkv); // the next step's first kernel
     LLMRS_TRY(mark(5));
     LLMRS_TRY(gemv_launch(m->lm_head.plan, h, PRO_NORM, EPI_ARGMAX, s, overlap));
     LLMRS_TRY(mark(-1));
@@ -1151,11 +1215,12 @@ int llmrs_model_trace_decode(llmrs_model *m, int token, int pos, unsigned long l
     if (!m->graph_traced)
         LLMRS_TRY(capture_step(m, &m->graph_traced, m->d_trace));
     cudaStream_t s = m->ctx->stream;
-    std::vector<unsigned long long> init((size_t)3 * nk);
+    std::vector<unsigned long long> init((size_t)TRACE_MARKS * nk);
     for (int i = 0; i < nk; i++) {
-        init[3 * i] = ~0ull;
-        init[3 * i + 1] = ~0ull;
-        init[3 * i + 2] = 0ull;
+        init[TRACE_MARKS * i] = ~0ull;     // min marks
+        init[TRACE_MARKS * i + 1] = ~0ull;
+        init[TRACE_MARKS * i + 2] = 0ull;  // max marks
+        init[TRACE_MARKS * i + 3] = 0ull;
     }
     LLMRS_CUDA_TRY(cudaMemcpyAsync(m->d_trace, init.data(), init.size() * 8, cudaMemcpyHostToDevice, s));
     LLMRS_TRY(set_token_pos(m, token, pos, 0));
