@@ -8,6 +8,9 @@ python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 One "step" = one greedy decode token through every layer + LM head.  Inputs
 (weights 4.2 GB, KV 1.1 GB) are far larger than the 126 MB L2, so no flush is
 needed between steps.  Synthetic seeded weights stand in for checkpoints.
+With N > 1 (torchrun, one rank per GPU) the model is tensor parallel over the N
+GPUs: one sequence, the same total work (strong scaling); the roofline's peak
+is then the N GPUs' aggregate HBM bandwidth.
 """
 import argparse
 import json
@@ -195,9 +198,12 @@ def run_ours(args, rank, world):
     if args.layers:
         c["n_layers"] = args.layers
     ctx = L.Context(local)
-    m = L.Model(ctx, c)
+    # N > 1: tensor parallel over the N GPUs (one sequence, strong scaling)
+    m = L.Model(ctx, dict(c, tp_rank=rank, tp_size=world))
     m.init_synthetic(SEED)
     m.kv_fill_synthetic(SEED, wl["kv"])
+    if world > 1:
+        L.connect_tensor_parallel(m)
     kv0 = wl["kv"]
     tok0 = 1234 % c["vocab"]
     K, W = args.steps, args.warmup
@@ -216,7 +222,7 @@ def run_ours(args, rank, world):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
     ms_per_step = ms / K
-    value = world * K / (ms / 1000.0)  # replicas: every rank decodes its own sequence
+    value = K / (ms / 1000.0)  # one sequence decoded by all ranks together
     # per-kernel durations (kernel by kernel, events around each launch)
     prof = [m.profile_decode(tok0, kv0 + i) for i in range(3)]
     per_kind = {}
@@ -230,14 +236,22 @@ def run_ours(args, rank, world):
     kind_count = {}
     for kind, _ in prof[0]:
         kind_count[kind] = kind_count.get(kind, 0) + 1
+    if world > 1:  # the slowest rank sets the pace
+        import torch
+        import torch.distributed as dist
+        names = sorted(kind_ms)
+        t = torch.tensor([kind_ms[k] for k in names], dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        kind_ms = {k: float(v) for k, v in zip(names, t.tolist())}
     gemv_kinds = [k for k in kind_ms if k.endswith("_gemv")]
     gemv_bytes_step = sum(gemv_bytes(k, c) * kind_count[k] for k in gemv_kinds)
     gemv_ms_step = sum(kind_ms[k] for k in gemv_kinds)
     gemv_launches = sum(kind_count[k] for k in gemv_kinds)
     traffic = None
-    if args.workload == "8b" and not args.layers:
+    if args.workload == "8b" and not args.layers and world == 1:
         traffic = round(sum(MEASURED_GEMV_DRAM_8B[k] * kind_count[k] for k in gemv_kinds) / gemv_launches)
     peak, peak_src = load_peaks()
+    peak *= world  # aggregate HBM bandwidth of the N GPUs
     achieved = gemv_bytes_step / (gemv_ms_step / 1000.0) / 1e9
     S_mid = kv0 + K // 2
     tot_bytes, w_bytes, kv_bytes = algo_bytes_per_token(c, S_mid)
@@ -250,7 +264,13 @@ def run_ours(args, rank, world):
     for i in range(E):
         tok, _ = m.decode_step(tok, kv0 + i, want_logits=False)
     e2e_s = time.perf_counter() - t0
-    e2e_val = world * E / e2e_s
+    if world > 1:
+        import torch
+        import torch.distributed as dist
+        t = torch.tensor([e2e_s], dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    e2e_val = E / e2e_s
     kernels_step = m.decode_kernel_count()
     out = {
         "metric": "batch-1 greedy decode tokens/s (Llama-3-8B-shaped Q4_0, KV 4096)" if args.workload == "8b"
@@ -262,12 +282,12 @@ def run_ours(args, rank, world):
         "warmup": W,
         "ms_per_step": round(ms_per_step, 4),
         "higher_is_better": True,
-        "scaling": "weak" if world > 1 else "strong",
+        "scaling": "strong",
         "vs_baseline": None,
         "dtype": "q4_0 x q8_0 (int8 dot, f32 accumulate), f32 KV",
         "data": "synthetic (seeded random-init weights of the named shape; KV pre-filled N(0,1))",
-        "config": {"workload": wl["name"], "model": args.workload, "global_batch": world, "seq_len": S_mid,
-                   "kv_prefill": kv0, "parallelism": "replicas%d" % world if world > 1 else "single",
+        "config": {"workload": wl["name"], "model": args.workload, "global_batch": 1, "seq_len": S_mid,
+                   "kv_prefill": kv0, "parallelism": "tp%d" % world,
                    "l2": "inputs larger than L2 (weights %.2f GB + KV %.2f GB per token)" % (w_bytes / 1e9,
                                                                                               kv_bytes / 1e9)},
         "roofline": {"bound": "hbm", "kernel": "gemv_tma_kernel (all Q4 GEMVs of one decode step)",
@@ -280,7 +300,7 @@ def run_ours(args, rank, world):
                      "step_frac": round(step_gbs / peak, 4)},
         "e2e": {"value": round(e2e_val, 2), "unit": "tokens/s", "h2d_bytes_per_step": 8,
                 "d2h_bytes_per_step": 8},
-        "gpu_launches": kernels_step * K,
+        "gpu_launches": world * kernels_step * K,
         "clocks": clk.summary(),
     }
     if rank == 0 and world == 1 and not args.no_cpu:

@@ -171,6 +171,13 @@ typedef struct {
     int scale_dtype;    /* LLMRS_F16: 18 B per 32 Q4 weights, every scale must be exactly
                            representable (synthetic models); LLMRS_F32: the reference's own
                            f32 scales (20 B per 32), e.g. for quantize_q4 of real checkpoints */
+    int tp_rank;        /* tensor parallel: this process's rank (0 for one GPU) */
+    int tp_size;        /* ranks (1, 2, 4 or 8; 0 = 1).  Rank r holds query/KV heads
+                           [r*n/tp, (r+1)*n/tp), FFN rows [r*ffn/tp, ...), the matching
+                           o_proj / down_proj input columns and LM-head rows
+                           [r*vocab/tp, ...); o_proj and down_proj outputs are summed
+                           across ranks over NVLink.  No counterpart in the reference
+                           (CPU / OpenCL, one device). */
 } llmrs_config;
 
 /* which-codes for llmrs_model_set_weight */
@@ -233,6 +240,25 @@ int llmrs_model_trace_decode(llmrs_model *model, int token, int pos, unsigned lo
 /* time `iters` device-resident decode steps (graph replays) with CUDA events
  * on the model's stream; *ms_total = elapsed ms; the KV position advances */
 int llmrs_model_time_decode(llmrs_model *model, int token, int pos, int iters, float *ms_total);
+
+/* ---- tensor parallel (one process per GPU; no counterpart in the reference) ----
+ * Each rank's model owns a communication region (partial sums of o_proj and
+ * down_proj from every rank, LM-head argmax keys, arrival counters).  Ranks
+ * exchange IPC handles of their regions (any host channel), open the others'
+ * and connect; decode calls then run on all ranks in the same order with the
+ * same token/position, every rank gets the same greedy token, and logits are
+ * the rank's vocab shard (vocab/tp floats).  A peer that stops answering
+ * makes the waiting kernel give up after ~5 s with LLMRS_EDEVICE. */
+#define LLMRS_IPC_HANDLE_BYTES 64
+/* the region of this rank (device pointer and size) */
+int llmrs_model_tp_region(llmrs_model *model, void **d_region, size_t *bytes);
+/* regions[q] = rank q's region as mapped in this process (regions[rank] = own) */
+int llmrs_model_tp_connect(llmrs_model *model, void *const *regions);
+/* CUDA IPC of a cudaMalloc'ed region: handle out (LLMRS_IPC_HANDLE_BYTES) */
+int llmrs_ipc_get_handle(const void *d_ptr, void *handle_out);
+/* map another process's region on `device` (peer access over NVLink) */
+int llmrs_ipc_open_handle(int device, const void *handle, void **d_ptr_out);
+int llmrs_ipc_close_handle(int device, void *d_ptr);
 
 #if defined(__GNUC__)
 #pragma GCC visibility pop

@@ -41,7 +41,10 @@ EXPORTS = [
     "llmrs_decode_step", "llmrs_generate", "llmrs_prefill", "llmrs_model_logits", "llmrs_rope_table",
     "llmrs_model_decode_kernel_count", "llmrs_model_time_decode", "llmrs_model_profile_decode",
     "llmrs_attention_decode", "llmrs_attention_decode_noalloc", "llmrs_model_trace_decode",
+    "llmrs_model_tp_region", "llmrs_model_tp_connect", "llmrs_ipc_get_handle", "llmrs_ipc_open_handle",
+    "llmrs_ipc_close_handle",
 ]
+IPC_HANDLE_BYTES = 64
 
 
 class LlmrsError(RuntimeError):
@@ -57,6 +60,7 @@ class Config(ctypes.Structure):
         ("vocab", ctypes.c_int), ("max_seq", ctypes.c_int), ("rms_eps", ctypes.c_float),
         ("rope_theta", ctypes.c_float), ("weight_format", ctypes.c_int),
         ("tied_embeddings", ctypes.c_int), ("scale_dtype", ctypes.c_int),
+        ("tp_rank", ctypes.c_int), ("tp_size", ctypes.c_int),
     ]
 
 
@@ -124,6 +128,11 @@ def lib():
         "llmrs_attention_decode": (ci, [vp, vp, vp, vp, vp, vp, vp, ci, ci, ci, ci, ci]),
         "llmrs_attention_decode_noalloc": (ci, [vp, vp, vp, vp, vp, vp, vp, ci, ci, ci, ci, ci, vp]),
         "llmrs_model_trace_decode": (ci, [vp, ci, ci, vp, vp, ip]),
+        "llmrs_model_tp_region": (ci, [vp, pp, ctypes.POINTER(sz)]),
+        "llmrs_model_tp_connect": (ci, [vp, pp]),
+        "llmrs_ipc_get_handle": (ci, [vp, vp]),
+        "llmrs_ipc_open_handle": (ci, [ci, vp, pp]),
+        "llmrs_ipc_close_handle": (ci, [ci, vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -364,6 +373,11 @@ class Model:
         self.ctx = ctx
         self.cfg = dict(cfg)
         self.cfg.setdefault("scale_dtype", F16)
+        self.cfg.setdefault("tp_rank", 0)
+        self.cfg.setdefault("tp_size", 1)
+        self.tp = max(1, int(self.cfg["tp_size"]))
+        self.vocab_local = self.cfg["vocab"] // self.tp
+        self._peer_maps = []
         c = Config(**{f: self.cfg[f] for f, _ in Config._fields_})
         h = ctypes.c_void_p()
         check(lib().llmrs_model_create(ctx.h, ctypes.byref(c), ctypes.byref(h)))
@@ -372,6 +386,9 @@ class Model:
 
     def close(self):
         if self.h and self.ctx.h:
+            for ptr in self._peer_maps:
+                lib().llmrs_ipc_close_handle(self.ctx.device, ptr)
+            self._peer_maps = []
             lib().llmrs_model_destroy(self.h)
         self.h = None
 
@@ -402,13 +419,13 @@ class Model:
 
     def kv_read(self, layer, n_pos):
         c = self.cfg
-        k = np.zeros((c["n_kv_heads"], n_pos, c["head_dim"]), np.float32)
+        k = np.zeros((c["n_kv_heads"] // self.tp, n_pos, c["head_dim"]), np.float32)
         v = np.zeros_like(k)
         check(lib().llmrs_kv_read(self.h, layer, _ptr(k), _ptr(v), n_pos))
         return k, v
 
     def decode_step(self, token, pos, want_logits=True):
-        logits = np.zeros(self.cfg["vocab"], np.float32) if want_logits else None
+        logits = np.zeros(self.vocab_local, np.float32) if want_logits else None
         am = ctypes.c_int(-1)
         check(lib().llmrs_decode_step(self.h, int(token), int(pos),
                                       None if logits is None else _ptr(logits), ctypes.byref(am)))
@@ -421,16 +438,42 @@ class Model:
 
     def prefill(self, ids, start_pos, want_logits=True):
         ids = np.ascontiguousarray(ids, np.int32)
-        logits = np.zeros(self.cfg["vocab"], np.float32) if want_logits else None
+        logits = np.zeros(self.vocab_local, np.float32) if want_logits else None
         am = ctypes.c_int(-1)
         check(lib().llmrs_prefill(self.h, _ptr(ids), ids.size, int(start_pos),
                                   None if logits is None else _ptr(logits), ctypes.byref(am)))
         return am.value, logits
 
     def logits(self):
-        out = np.zeros(self.cfg["vocab"], np.float32)
+        out = np.zeros(self.vocab_local, np.float32)
         check(lib().llmrs_model_logits(self.h, _ptr(out)))
         return out
+
+    # ---- tensor parallel: one process per GPU
+    def tp_handle(self):
+        """IPC handle (bytes) of this rank's communication region."""
+        ptr, n = ctypes.c_void_p(), ctypes.c_size_t()
+        check(lib().llmrs_model_tp_region(self.h, ctypes.byref(ptr), ctypes.byref(n)))
+        hbuf = ctypes.create_string_buffer(IPC_HANDLE_BYTES)
+        check(lib().llmrs_ipc_get_handle(ptr, hbuf))
+        return hbuf.raw, ptr.value
+
+    def tp_connect(self, handles):
+        """handles[q] = rank q's tp_handle()[0]; maps the peers' regions (over
+        NVLink) and links the model to them."""
+        rank = self.cfg["tp_rank"]
+        own = self.tp_handle()[1]
+        regions = (ctypes.c_void_p * self.tp)()
+        for q, hb in enumerate(handles):
+            if q == rank:
+                regions[q] = own
+                continue
+            ptr = ctypes.c_void_p()
+            check(lib().llmrs_ipc_open_handle(self.ctx.device, ctypes.create_string_buffer(hb, IPC_HANDLE_BYTES),
+                                              ctypes.byref(ptr)))
+            self._peer_maps.append(ptr.value)
+            regions[q] = ptr.value
+        check(lib().llmrs_model_tp_connect(self.h, regions))
 
     def decode_kernel_count(self):
         n = ctypes.c_int(0)
@@ -467,3 +510,15 @@ class Model:
         ms = ctypes.c_float(0)
         check(lib().llmrs_model_time_decode(self.h, int(token), int(pos), int(iters), ctypes.byref(ms)))
         return ms.value
+
+
+def connect_tensor_parallel(model, group=None):
+    """Exchange the ranks' IPC handles over torch.distributed (any backend;
+    host plumbing only) and connect `model`; every rank calls this once."""
+    import torch.distributed as dist
+
+    handle, _ = model.tp_handle()
+    handles = [None] * dist.get_world_size(group)
+    dist.all_gather_object(handles, handle, group=group)
+    model.tp_connect(handles)
+    dist.barrier(group)

@@ -25,7 +25,6 @@
 
 #include "attention.cuh"
 #include "common.cuh"
-#include "prefetch.cuh"
 
 namespace llmrs {
 
@@ -249,8 +248,6 @@ __global__ void __launch_bounds__(AttnWarps<D>::value * 32, 1) attn_decode_kerne
         const uint64_t pol = policy_evict_first();
         for (int j = 0; j < 2 && j < mine; j++)
             issue(j, pol);
-        if (warp == NW - 1)
-            issue_next_prefetch(p.pf, blockIdx.y * gridDim.x + blockIdx.x, gridDim.x * gridDim.y);
     }
     __syncwarp();
     if (warp < NREP) { // RoPE(q) of head `warp` into shared memory

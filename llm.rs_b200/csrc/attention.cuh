@@ -24,7 +24,6 @@ struct AttnParams {
     int trace_slot;
     int n_heads, n_kv, head_dim, max_seq, n_splits;
     float inv_sqrt_d;        // 1 / sqrt(D), as src/core/layer.rs:258 computes it
-    NextPrefetch pf;         // the next kernel's first bytes (PF_NONE: nothing)
 };
 
 int attention_decode_launch(const AttnParams &p, cudaStream_t stream, bool pdl);

@@ -109,24 +109,6 @@ __device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, i
         : "memory");
 }
 
-// bulk prefetch of [p, p + bytes) into L2 (16-byte aligned, multiple of 16)
-__device__ __forceinline__ void prefetch_l2(const void *p, uint32_t bytes)
-{
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
-}
-
-// prefetch an arbitrary byte range, rounded inward to 16-byte units, in
-// pieces of at most 64 KB
-__device__ __forceinline__ void prefetch_l2_range(const uint8_t *p, size_t bytes)
-{
-    const uintptr_t a0 = ((uintptr_t)p + 15) & ~(uintptr_t)15;
-    const uintptr_t a1 = ((uintptr_t)p + bytes) & ~(uintptr_t)15;
-    for (uintptr_t a = a0; a < a1; a += 65536) {
-        const uintptr_t n = a1 - a < 65536 ? a1 - a : 65536;
-        prefetch_l2(reinterpret_cast<const void *>(a), (uint32_t)n);
-    }
-}
-
 // order this thread's earlier generic-proxy shared-memory accesses before its
 // later async-proxy (bulk copy) accesses of the same bytes
 __device__ __forceinline__ void fence_proxy_async_smem()
@@ -164,6 +146,36 @@ __device__ __forceinline__ uint64_t globaltimer_ns()
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     return t;
 }
+
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long *p)
+{
+    unsigned long long v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Wait until *c >= target (a counter other GPUs raise over NVLink); gives up
+// after limit_ns, records DEV_ERR_PEER_TIMEOUT and returns false.
+__device__ __forceinline__ bool wait_counter(const unsigned long long *c, unsigned long long target, uint32_t *err,
+                                             uint64_t limit_ns = 5000000000ull)
+{
+    if (ld_acquire_sys(c) >= target)
+        return true;
+    if (err && *reinterpret_cast<volatile uint32_t *>(err) != 0)
+        return false; // an earlier wait of this step already gave up: do not wait again
+    const uint64_t t0 = globaltimer_ns();
+    for (;;) {
+        __nanosleep(64);
+        if (ld_acquire_sys(c) >= target)
+            return true;
+        if (globaltimer_ns() - t0 > limit_ns) {
+            if (err)
+                atomicCAS(err, 0u, (uint32_t)DEV_ERR_PEER_TIMEOUT);
+            return false;
+        }
+    }
+}
+
 
 // Wait for the given phase parity; gives up after ~limit_ns and records the
 // timeout in *err.  Returns false on timeout.

@@ -40,7 +40,6 @@
 
 #include "common.cuh"
 #include "gemv.cuh"
-#include "prefetch.cuh"
 
 // Optional phase tracing (cycle counters around pipeline waits); compiled out
 // unless a tracing build defines LLMRS_GEMV_TRACE and provides the hooks.
@@ -136,6 +135,19 @@ __device__ __forceinline__ void quantize_pack(const float (&v)[32], uint32_t *ds
     *dst_c = WF == 0 ? -8 * sum : 0;
 }
 
+// 32 floats through L2 only (data other GPUs wrote into this GPU's memory)
+__device__ __forceinline__ void load32_cg(const float *src, float (&v)[32])
+{
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        const float4 t = __ldcg(reinterpret_cast<const float4 *>(src) + j);
+        v[4 * j] = t.x;
+        v[4 * j + 1] = t.y;
+        v[4 * j + 2] = t.z;
+        v[4 * j + 3] = t.w;
+    }
+}
+
 __device__ __forceinline__ void load32(const float *src, float (&v)[32])
 {
     const float4 *s4 = reinterpret_cast<const float4 *>(src);
@@ -221,7 +233,8 @@ __device__ void load_activation(const GemvParams &p, uint32_t *act, float *act_s
         }
         return;
     }
-    constexpr bool NORM = PRO == PRO_NORM || PRO == PRO_EMBED_NORM;
+    constexpr bool NORM = PRO == PRO_NORM || PRO == PRO_EMBED_NORM || PRO == PRO_AR_NORM;
+    constexpr bool AR = PRO == PRO_AR_NORM;
     const float *x = p.x;
     if (PRO == PRO_EMBED_NORM) {
         int tok = p.state->token;
@@ -232,21 +245,58 @@ __device__ void load_activation(const GemvParams &p, uint32_t *act, float *act_s
         }
         x = p.embed + (size_t)tok * K;
     }
+    const float *part = nullptr; // AR: this rank's receive buffer [size][K]
+    int nparts = 0;
+    if (AR) {
+        // the weight stream need not wait for the other ranks
+        signal_issued(issued, tid);
+        const TpLink *tp = p.tp;
+        if (tid == 0) {
+            const unsigned long long target =
+                ((unsigned long long)p.state->epoch * p.ar_per_step + p.ar_index + 1) * (unsigned long long)p.ar_arrivals;
+            wait_counter(tp->cnt[tp->rank] + p.ar_kind, target, p.err);
+        }
+        named_bar_sync(bar, nthr);
+        part = tp->ar[p.ar_kind][tp->rank];
+        nparts = tp->size;
+    }
+    // block b of the input: x, or (AR) the ranks' partial sums in rank order, then + x
+    auto load_x = [&](int b, float (&u)[32]) {
+        load32(x + (size_t)b * 32, u);
+        if (AR) {
+            float t[32];
+            load32_cg(part + (size_t)b * 32, t);
+            for (int q = 1; q < nparts; q++) {
+                float w[32];
+                load32_cg(part + (size_t)q * K + (size_t)b * 32, w);
+#pragma unroll
+                for (int i = 0; i < 32; i++)
+                    t[i] = __fadd_rn(t[i], w[i]);
+            }
+#pragma unroll
+            for (int i = 0; i < 32; i++)
+                u[i] = __fadd_rn(t[i], u[i]);
+        }
+    };
     float v[32], wn[32];
     if (has) {
-        load32(x + (size_t)tid * 32, v);
+        load_x(tid, v);
         if (NORM)
             load32(p.norm_w + (size_t)tid * 32, wn);
     }
-    signal_issued(issued, tid);
-    if (PRO == PRO_EMBED_NORM && blockIdx.x == 0) { // the residual stream starts as the embedding row
+    if (!AR)
+        signal_issued(issued, tid);
+    if ((PRO == PRO_EMBED_NORM || AR) && blockIdx.x == 0) { // the residual stream's new value
         if (has)
 #pragma unroll
             for (int i = 0; i < 32; i++)
                 p.x_out[(size_t)tid * 32 + i] = v[i];
-        for (int b = tid + nthr; b < nb; b += nthr)
+        for (int b = tid + nthr; b < nb; b += nthr) {
+            float u[32];
+            load_x(b, u);
             for (int i = 0; i < 32; i++)
-                p.x_out[(size_t)b * 32 + i] = x[(size_t)b * 32 + i];
+                p.x_out[(size_t)b * 32 + i] = u[i];
+        }
     }
     float scale = 1.0f;
     if (NORM) {
@@ -258,7 +308,7 @@ __device__ void load_activation(const GemvParams &p, uint32_t *act, float *act_s
                 ss = __fadd_rn(ss, __fmul_rn(v[i], v[i]));
         for (int b = tid + nthr; b < nb; b += nthr) {
             float u[32];
-            load32(x + (size_t)b * 32, u);
+            load_x(b, u);
 #pragma unroll
             for (int i = 0; i < 32; i++)
                 ss = __fadd_rn(ss, __fmul_rn(u[i], u[i]));
@@ -283,7 +333,7 @@ __device__ void load_activation(const GemvParams &p, uint32_t *act, float *act_s
     }
     for (int b = tid + nthr; b < nb; b += nthr) {
         float u[32];
-        load32(x + (size_t)b * 32, u);
+        load_x(b, u);
         if (NORM) {
             float un[32];
             load32(p.norm_w + (size_t)b * 32, un);
@@ -293,6 +343,27 @@ __device__ void load_activation(const GemvParams &p, uint32_t *act, float *act_s
         }
         quantize_pack<WF>(u, act + (size_t)b * 8, act_s + b, act_c + b);
     }
+}
+
+// Tensor parallel: this CTA's partial rows are in every rank's buffer; count
+// the CTA in on every rank.  The barrier orders every thread's stores before
+// thread 0's system-scope fence (cumulativity), which orders them before the
+// counter increments the other ranks acquire.
+__device__ __forceinline__ void partial_signal(const GemvParams &p, int tid, int nthr, int bar)
+{
+    named_bar_sync(bar, nthr);
+    if (tid == 0) {
+        __threadfence_system();
+        for (int q = 0; q < p.tp->size; q++)
+            atomicAdd_system(p.tp->cnt[q] + p.ar_kind, 1ull);
+    }
+}
+
+__device__ __forceinline__ void partial_store(const GemvParams &p, int row, float acc)
+{
+    const size_t off = (size_t)p.tp->rank * p.N + row;
+    for (int q = 0; q < p.tp->size; q++)
+        p.tp->ar[p.ar_kind][q][off] = acc;
 }
 
 // ------------------------------------------------------------- block dots
@@ -365,9 +436,23 @@ __device__ void argmax_finalize(const GemvParams &p, unsigned long long key, int
         const unsigned int ticket = atomicAdd(&p.state->done, 1u);
         if (ticket == gridDim.x - 1) {
             __threadfence();
-            const unsigned long long best = atomicAdd(&p.state->key, 0ull);
-            const int tok = (int)argmax_key_index(best);
+            unsigned long long best = atomicAdd(&p.state->key, 0ull);
             StepState *st = p.state;
+            const unsigned long long epoch = st->epoch;
+            if (p.tp && p.tp->size > 1) { // every rank holds a vocab shard: exchange the best keys
+                const TpLink *tp = p.tp;
+                for (int q = 0; q < tp->size; q++)
+                    tp->keys[q][tp->rank] = best;
+                __threadfence_system();
+                for (int q = 0; q < tp->size; q++)
+                    atomicAdd_system(tp->cnt[q] + TP_CNT_KEY, 1ull);
+                if (wait_counter(tp->cnt[tp->rank] + TP_CNT_KEY, (epoch + 1) * (unsigned long long)tp->size, p.err))
+                    for (int q = 0; q < tp->size; q++) {
+                        const unsigned long long k = __ldcg(tp->keys[tp->rank] + q);
+                        best = k > best ? k : best;
+                    }
+            }
+            const int tok = (int)argmax_key_index(best);
             const int n = st->n_log;
             if (p.token_log && n < st->log_cap)
                 p.token_log[n] = tok;
@@ -376,6 +461,7 @@ __device__ void argmax_finalize(const GemvParams &p, unsigned long long key, int
             st->pos = st->pos + 1;
             st->key = 0ull;
             st->done = 0u;
+            st->epoch = epoch + 1;
             __threadfence();
         }
     }
@@ -494,7 +580,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     }
                 }
             }
-            issue_next_prefetch(p.pf, blockIdx.x, gridDim.x);
             LLMRS_TRACE_FLUSH(1);
         }
         return;
@@ -648,9 +733,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 if (valid) {
                     if (p.y)
                         p.y[row] = acc;
-                    const unsigned long long k = argmax_key(acc, (uint32_t)row);
+                    const unsigned long long k = argmax_key(acc, (uint32_t)(row + p.row_offset));
                     best = k > best ? k : best;
                 }
+            } else if (EPI == EPI_PARTIAL) {
+                if (valid)
+                    partial_store(p, row, acc);
             }
         }
     }
@@ -661,6 +749,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         steps(std::integral_constant<int, 2>{});
     else
         steps(std::integral_constant<int, 4>{});
+    if (EPI == EPI_PARTIAL)
+        partial_signal(p, ctid, PRO_THREADS, 1);
     if (EPI == EPI_ARGMAX)
         argmax_finalize(p, best, ctid, PRO_THREADS, 1);
     LLMRS_TRACE_FLUSH(0);
@@ -725,9 +815,13 @@ __global__ void __launch_bounds__(SIMPLE_THREADS) gemv_simple_kernel(const GemvP
         } else if (EPI == EPI_ARGMAX) {
             if (p.y)
                 p.y[row] = acc;
-            best = argmax_key(acc, (uint32_t)row);
+            best = argmax_key(acc, (uint32_t)(row + p.row_offset));
+        } else if (EPI == EPI_PARTIAL) {
+            partial_store(p, row, acc);
         }
     }
+    if (EPI == EPI_PARTIAL)
+        partial_signal(p, threadIdx.x, SIMPLE_THREADS, 1);
     if (EPI == EPI_SILU) {
         // rows (2i, 2i+1) are threads (2i, 2i+1) of this block
         __shared__ float rows_acc[SIMPLE_THREADS];
@@ -880,7 +974,13 @@ int gemv_plan(GemvPlan *plan, const void *w, const void *scales, int N, int K, i
     X(1, 1, PRO_F32, EPI_STORE) X(1, 1, PRO_NORM, EPI_STORE) X(1, 1, PRO_EMBED_NORM, EPI_STORE)            \
     X(1, 1, PRO_F32, EPI_RESIDUAL) X(1, 1, PRO_NORM, EPI_SILU) X(1, 1, PRO_NORM, EPI_ARGMAX)               \
     X(0, 0, PRO_Q8, EPI_RESIDUAL) X(0, 1, PRO_Q8, EPI_RESIDUAL) X(1, 0, PRO_Q8, EPI_RESIDUAL)             \
-    X(1, 1, PRO_Q8, EPI_RESIDUAL)
+    X(1, 1, PRO_Q8, EPI_RESIDUAL)                                                                          \
+    X(0, 0, PRO_F32, EPI_PARTIAL) X(0, 0, PRO_AR_NORM, EPI_STORE) X(0, 0, PRO_AR_NORM, EPI_SILU)           \
+    X(0, 0, PRO_AR_NORM, EPI_ARGMAX) X(0, 1, PRO_F32, EPI_PARTIAL) X(0, 1, PRO_AR_NORM, EPI_STORE)         \
+    X(0, 1, PRO_AR_NORM, EPI_SILU) X(0, 1, PRO_AR_NORM, EPI_ARGMAX) X(1, 0, PRO_F32, EPI_PARTIAL)          \
+    X(1, 0, PRO_AR_NORM, EPI_STORE) X(1, 0, PRO_AR_NORM, EPI_SILU) X(1, 0, PRO_AR_NORM, EPI_ARGMAX)        \
+    X(1, 1, PRO_F32, EPI_PARTIAL) X(1, 1, PRO_AR_NORM, EPI_STORE) X(1, 1, PRO_AR_NORM, EPI_SILU)           \
+    X(1, 1, PRO_AR_NORM, EPI_ARGMAX)
 
 int gemv_launch(const GemvPlan &plan, const GemvParams &p, int pro, int epi, cudaStream_t stream, bool pdl)
 {
@@ -893,6 +993,11 @@ int gemv_launch(const GemvPlan &plan, const GemvParams &p, int pro, int epi, cud
     LLMRS_GEMV_VARIANTS(LLMRS_GEMV_CASE)
 #undef LLMRS_GEMV_CASE
     return fail(LLMRS_ENOTSUP, "gemv: unsupported variant wf=%d st=%d pro=%d epi=%d", wf, st, pro, epi);
+}
+
+int gemv_grid(const GemvPlan &plan)
+{
+    return plan.fast ? plan.grid : (plan.N + SIMPLE_THREADS - 1) / SIMPLE_THREADS;
 }
 
 int gemv_prefetch_stages(void)

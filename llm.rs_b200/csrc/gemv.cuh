@@ -14,6 +14,8 @@ enum GemvPro : int {
     PRO_NORM = 1,       // RMSNorm(x, norm_w) -> Q8_0
     PRO_EMBED_NORM = 2, // x = embed[*token] (CTA 0 stores it to x_out) -> RMSNorm -> Q8_0
     PRO_Q8 = 3,         // pre-quantised codes xq [K] + scales xs [K/32]
+    PRO_AR_NORM = 4,    // tensor parallel: x = (sum of every rank's partial) + x (CTA 0 stores it to
+                        // x_out) once all partials arrived -> RMSNorm -> Q8_0
 };
 
 // output epilogues
@@ -22,6 +24,18 @@ enum GemvEpi : int {
     EPI_RESIDUAL = 1, // y[row] = acc + residual[row]   (y may alias residual)
     EPI_SILU = 2,     // rows (2i, 2i+1) = (gate_i, up_i): y[i] = silu(gate_i) * up_i
     EPI_ARGMAX = 3,   // y[row] = acc; greedy argmax over all rows -> step state
+    EPI_PARTIAL = 4,  // tensor parallel: acc -> every rank's partial buffer, then count the CTA in
+};
+
+// Tensor-parallel links of one rank: pointers into every rank's communication
+// region (this rank's own included), mapped over NVLink.
+constexpr int TP_MAX = 8;
+enum TpCounter : int { TP_CNT_O = 0, TP_CNT_DOWN = 1, TP_CNT_KEY = 2, TP_CNT_N = 4 };
+struct TpLink {
+    int rank = 0, size = 1;
+    float *ar[2][TP_MAX] = {};            // [o / down][rank q]: q's receive buffer [size][N], block r from rank r
+    unsigned long long *cnt[TP_MAX] = {}; // [rank q]: q's arrival counters [TP_CNT_N]
+    unsigned long long *keys[TP_MAX] = {}; // [rank q]: q's argmax key slots [size]
 };
 
 struct StepState {
@@ -33,27 +47,7 @@ struct StepState {
     int n_log;               // tokens appended to the log so far
     int log_cap;             // capacity of the token log
     int pad;
-};
-
-// What the next kernel of a decode step reads first, prefetched into L2 by the
-// current kernel once its own stream is requested: the HBM keeps streaming
-// through the current kernel's tail, the launch gap and the next prologue.
-enum NextPrefetchKind : int {
-    PF_NONE = 0,
-    PF_ROWS = 1, // next is a GEMV: CTA j -> [a + j*a_stride, +a_bytes) and [b + j*b_stride, +b_bytes)
-    PF_KV = 2,   // next is decode attention: CTA j -> split j % n_splits of KV head j / n_splits
-};
-
-struct NextPrefetch {
-    int kind = PF_NONE;
-    int ncta = 0;                      // CTAs of the next kernel that get a range
-    const uint8_t *a = nullptr, *b = nullptr;
-    size_t a_stride = 0, a_bytes = 0, a_end = 0; // a_end, b_end: bytes of the whole tensor
-    size_t b_stride = 0, b_bytes = 0, b_end = 0;
-    const float *kc = nullptr, *vc = nullptr;    // PF_KV
-    const StepState *state = nullptr;            // PF_KV: decode position
-    int max_seq = 0, head_dim = 0, n_splits = 0;
-    size_t kv_bytes = 0;               // PF_KV: cap per K or V range
+    unsigned long long epoch; // decode steps completed (tensor-parallel counter targets)
 };
 
 struct GemvParams {
@@ -81,7 +75,13 @@ struct GemvParams {
     int rows_per_cta;
     unsigned long long *trace; // optional timeline marks, 3 per kernel (see trace_start)
     int trace_slot;
-    NextPrefetch pf;       // the next kernel's first bytes (PF_NONE: nothing)
+    // tensor parallel (EPI_PARTIAL, PRO_AR_NORM, EPI_ARGMAX over a vocab shard)
+    const TpLink *tp;      // nullptr: one GPU
+    int ar_kind;           // TP_CNT_O / TP_CNT_DOWN
+    int ar_index;          // all-reduce instance within the step (layer)
+    int ar_per_step;       // instances of this kind per step
+    int ar_arrivals;       // counter increments per instance (ranks x producer CTAs)
+    int row_offset;        // EPI_ARGMAX: global index of local row 0
 };
 
 // Launch geometry + TMA descriptors of one weight matrix, built once per weight.
@@ -105,6 +105,8 @@ int gemv_launch(const GemvPlan &plan, const GemvParams &p, int pro, int epi, cud
 // set kernel attributes (dynamic smem limits) for every variant on the current device;
 // called once per context, outside any stream capture
 int gemv_prepare(void);
+// CTAs a launch of this plan uses
+int gemv_grid(const GemvPlan &plan);
 // weight stages a GEMV streams before its activation loads are issued
 // (LLMRS_GEMV_PREFETCH, default 0)
 int gemv_prefetch_stages(void);

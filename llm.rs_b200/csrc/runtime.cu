@@ -116,6 +116,13 @@ int check_cfg(const llmrs_config *c)
                     "config: tied embeddings require Q4_0 (quantize_q4 of the embedding)");
     LLMRS_CHECK_ARG(c->scale_dtype == LLMRS_F16 || c->scale_dtype == LLMRS_F32, "config: scale_dtype %d unknown",
                     c->scale_dtype);
+    const int T = c->tp_size > 0 ? c->tp_size : 1;
+    LLMRS_CHECK_ARG(T == 1 || T == 2 || T == 4 || T == 8, "config: tp_size %d not 1, 2, 4 or 8", c->tp_size);
+    LLMRS_CHECK_ARG(c->tp_rank >= 0 && c->tp_rank < T, "config: tp_rank %d outside [0,%d)", c->tp_rank, T);
+    LLMRS_CHECK_ARG(c->n_kv_heads % T == 0 && c->vocab % T == 0 && (c->ffn / T) % 32 == 0 &&
+                        (c->n_heads / T * c->head_dim) % 32 == 0,
+                    "config: n_kv_heads, vocab, ffn/32 and n_heads*head_dim/32 must split over tp_size %d", T);
+    LLMRS_CHECK_ARG(T == 1 || !c->tied_embeddings || (c->vocab / T) % 1 == 0, "config: bad vocab shard");
     return LLMRS_OK;
 }
 
@@ -125,7 +132,10 @@ struct llmrs_model {
     llmrs_ctx *ctx = nullptr;
     llmrs_config cfg{};
     int wf = 0, st = 0;
-    int D = 0, Hq = 0, Hkv = 0, H = 0, F = 0, V = 0, S = 0;
+    // Hq, Hkv, F: this rank's shard (the whole model for one GPU); V: full vocab,
+    // Vl: this rank's LM-head rows
+    int D = 0, Hq = 0, Hkv = 0, H = 0, F = 0, V = 0, Vl = 0, S = 0;
+    int T = 1, rank = 0;
     Arena arena;
     std::vector<LayerW> layers;
     float *embed = nullptr, *final_norm = nullptr;
@@ -133,6 +143,12 @@ struct llmrs_model {
     float *rope_cos = nullptr, *rope_sin = nullptr;
     // activations
     float *x = nullptr, *qkv = nullptr, *ctxv = nullptr, *act = nullptr, *logits = nullptr, *part = nullptr;
+    float *x1 = nullptr; // tensor parallel: second residual buffer (o_proj all-reduce target)
+    // tensor parallel: communication region (own cudaMalloc, shared over IPC) and links
+    void *tp_region = nullptr;
+    size_t tp_bytes = 0, tp_off_o = 0, tp_off_d = 0, tp_off_keys = 0, tp_off_cnt = 0;
+    TpLink *d_tp = nullptr;
+    bool tp_connected = false;
     unsigned int *att_counter = nullptr;
     StepState *state = nullptr;
     int *token_log = nullptr;
@@ -495,6 +511,8 @@ static void model_free(llmrs_model *m)
         cudaGraphExecDestroy(m->graph_traced);
     if (m->arena.base)
         cudaFree(m->arena.base);
+    if (m->tp_region)
+        cudaFree(m->tp_region);
     if (m->h_stage)
         cudaFreeHost(m->h_stage);
     delete m;
@@ -511,16 +529,20 @@ int llmrs_model_create(llmrs_ctx *ctx, const llmrs_config *cfg, llmrs_model **ou
     m->cfg = *cfg;
     m->wf = cfg->weight_format;
     m->st = cfg->scale_dtype;
+    m->T = cfg->tp_size > 0 ? cfg->tp_size : 1;
+    m->rank = cfg->tp_rank;
+    m->cfg.tp_size = m->T;
     m->D = cfg->head_dim;
-    m->Hq = cfg->n_heads;
-    m->Hkv = cfg->n_kv_heads;
+    m->Hq = cfg->n_heads / m->T;
+    m->Hkv = cfg->n_kv_heads / m->T;
     m->H = cfg->hidden;
-    m->F = cfg->ffn;
+    m->F = cfg->ffn / m->T;
     m->V = cfg->vocab;
+    m->Vl = cfg->vocab / m->T;
     m->S = cfg->max_seq;
     m->n_splits = attention_default_splits(m->Hkv);
     m->log_cap = 1 << 16;
-    const int D = m->D, H = m->H, F = m->F, V = m->V, S = m->S;
+    const int D = m->D, H = m->H, F = m->F, V = m->V, Vl = m->Vl, S = m->S;
     const size_t qkv_rows = (size_t)(m->Hq + 2 * m->Hkv) * D;
     const size_t qdim = (size_t)m->Hq * D;
     const int wf = m->wf;
@@ -534,12 +556,13 @@ int llmrs_model_create(llmrs_ctx *ctx, const llmrs_config *cfg, llmrs_model **ou
     }
     total += (size_t)V * H * 4 + 256;                                       // embed
     total += (size_t)H * 4 + 256;                                           // final norm
-    total += (cfg->tied_embeddings ? (size_t)V * H / 2 : wbytes(wf, V, H)) + (size_t)V * H / 32 * 4 + 512;
+    total += (cfg->tied_embeddings ? (size_t)Vl * H / 2 : wbytes(wf, Vl, H)) + (size_t)Vl * H / 32 * 4 + 512;
     total += 2 * (size_t)S * D / 2 * 4 + 512;                              // rope
-    total += ((size_t)H + qkv_rows + qdim + F + V) * 4 + 5 * 256;           // activations
+    total += ((size_t)2 * H + qkv_rows + qdim + F + Vl) * 4 + 6 * 256;       // activations
+    total += sizeof(TpLink) + 256;
     total += attention_partials_floats(m->Hq, D, m->n_splits) * 4 + 256;
     total += (size_t)m->Hkv * 4 + sizeof(StepState) + (size_t)m->log_cap * 4 + 1024;
-    total += (size_t)3 * (5 * cfg->n_layers + 8) * 8 + 256; // timeline marks
+    total += (size_t)TRACE_MARKS * (5 * cfg->n_layers + 8) * 8 + 256; // timeline marks
     cudaError_t e = cudaMalloc(&m->arena.base, total);
     if (e != cudaSuccess) {
         model_free(m);
@@ -568,13 +591,13 @@ int llmrs_model_create(llmrs_ctx *ctx, const llmrs_config *cfg, llmrs_model **ou
     m->embed = (float *)A.take((size_t)V * H * 4);
     m->final_norm = (float *)A.take((size_t)H * 4);
     if (cfg->tied_embeddings) {
-        m->lm_head.n = V;
+        m->lm_head.n = Vl;
         m->lm_head.k = H;
         m->lm_head.st = LLMRS_F32;
-        m->lm_head.w = (uint8_t *)A.take((size_t)V * H / 2);
-        m->lm_head.s = A.take((size_t)V * H / 32 * 4);
+        m->lm_head.w = (uint8_t *)A.take((size_t)Vl * H / 2);
+        m->lm_head.s = A.take((size_t)Vl * H / 32 * 4);
     } else {
-        mkq(m->lm_head, V, H, m->st);
+        mkq(m->lm_head, Vl, H, m->st);
     }
     m->rope_cos = (float *)A.take((size_t)S * D / 2 * 4);
     m->rope_sin = (float *)A.take((size_t)S * D / 2 * 4);
@@ -582,13 +605,15 @@ int llmrs_model_create(llmrs_ctx *ctx, const llmrs_config *cfg, llmrs_model **ou
     m->qkv = (float *)A.take(qkv_rows * 4);
     m->ctxv = (float *)A.take(qdim * 4);
     m->act = (float *)A.take((size_t)F * 4);
-    m->logits = (float *)A.take((size_t)V * 4);
+    m->logits = (float *)A.take((size_t)Vl * 4);
+    m->x1 = (float *)A.take((size_t)H * 4);
+    m->d_tp = (TpLink *)A.take(sizeof(TpLink));
     m->part = (float *)A.take(attention_partials_floats(m->Hq, D, m->n_splits) * 4);
     m->att_counter = (unsigned int *)A.take((size_t)m->Hkv * 4);
     m->state = (StepState *)A.take(sizeof(StepState));
     m->token_log = (int *)A.take((size_t)m->log_cap * 4);
     m->d_trace = (unsigned long long *)A.take((size_t)TRACE_MARKS * (5 * cfg->n_layers + 8) * 8);
-    if (!m->token_log || !m->d_trace) {
+    if (!m->token_log || !m->d_trace || !m->d_tp) {
         model_free(m);
         return fail(LLMRS_ENOMEM, "model arena layout overflow");
     }
@@ -630,6 +655,18 @@ int llmrs_model_create(llmrs_ctx *ctx, const llmrs_config *cfg, llmrs_model **ou
         st0.log_cap = m->log_cap;
         e = cudaMemcpyAsync(m->state, &st0, sizeof(st0), cudaMemcpyHostToDevice, s);
     }
+    if (e == cudaSuccess && m->T > 1) {
+        // communication region: partials [T][H] for o_proj and down_proj, keys [T], counters
+        auto up = [](size_t v) { return (v + 255) & ~size_t(255); };
+        m->tp_off_o = 0;
+        m->tp_off_d = up((size_t)m->T * H * 4);
+        m->tp_off_keys = m->tp_off_d + up((size_t)m->T * H * 4);
+        m->tp_off_cnt = m->tp_off_keys + up((size_t)m->T * 8);
+        m->tp_bytes = m->tp_off_cnt + up((size_t)TP_CNT_N * 8);
+        e = cudaMalloc(&m->tp_region, m->tp_bytes);
+        if (e == cudaSuccess)
+            e = cudaMemsetAsync(m->tp_region, 0, m->tp_bytes, s);
+    }
     if (e == cudaSuccess)
         e = cudaStreamSynchronize(s);
     if (e != cudaSuccess) {
@@ -663,28 +700,36 @@ int llmrs_model_init_synthetic(llmrs_model *m, uint64_t seed)
     LLMRS_CHECK_ARG(m->st == LLMRS_F16 || m->st == LLMRS_F32, "bad scale dtype");
     cudaSetDevice(m->ctx->device);
     cudaStream_t s = m->ctx->stream;
-    const int D = m->D, H = m->H, F = m->F, V = m->V;
-    const int qd = m->Hq * D, kd = m->Hkv * D;
+    const int D = m->D, H = m->H, F = m->F, V = m->V, Vl = m->Vl, r = m->rank;
+    const int qd = m->Hq * D, kd = m->Hkv * D; // this rank's rows
+    const int QD = qd * m->T, FF = F * m->T;   // full o_proj / down_proj input widths
     for (int l = 0; l < m->cfg.n_layers; l++) {
         LayerW &L = m->layers[l];
-        // fused QKV rows: q | k | v (native GQA)
-        LLMRS_TRY(synth_quant(s, m->wf, seed, l, LLMRS_T_Q, H, 0, qd, 0, H, L.qkv.w, L.qkv.s, L.qkv.st, 1, 0));
-        LLMRS_TRY(synth_quant(s, m->wf, seed, l, LLMRS_T_K, H, 0, kd, 0, H, L.qkv.w, L.qkv.s, L.qkv.st, 1, qd));
-        LLMRS_TRY(synth_quant(s, m->wf, seed, l, LLMRS_T_V, H, 0, kd, 0, H, L.qkv.w, L.qkv.s, L.qkv.st, 1, qd + kd));
-        LLMRS_TRY(synth_quant(s, m->wf, seed, l, LLMRS_T_O, qd, 0, H, 0, qd, L.o.w, L.o.s, L.o.st, 1, 0));
-        // gate/up interleaved: device row 2i = gate i, 2i+1 = up i
-        LLMRS_TRY(synth_quant(s, m->wf, seed, l, LLMRS_T_GATE, H, 0, F, 0, H, L.gate_up.w, L.gate_up.s, L.gate_up.st, 2, 0));
-        LLMRS_TRY(synth_quant(s, m->wf, seed, l, LLMRS_T_UP, H, 0, F, 0, H, L.gate_up.w, L.gate_up.s, L.gate_up.st, 2, 1));
-        LLMRS_TRY(synth_quant(s, m->wf, seed, l, LLMRS_T_DOWN, F, 0, H, 0, F, L.down.w, L.down.s, L.down.st, 1, 0));
+        // fused QKV rows: q | k | v (native GQA); rank r: its heads' rows
+        LLMRS_TRY(synth_quant(s, m->wf, seed, l, LLMRS_T_Q, H, r * qd, qd, 0, H, L.qkv.w, L.qkv.s, L.qkv.st, 1, 0));
+        LLMRS_TRY(synth_quant(s, m->wf, seed, l, LLMRS_T_K, H, r * kd, kd, 0, H, L.qkv.w, L.qkv.s, L.qkv.st, 1, qd));
+        LLMRS_TRY(synth_quant(s, m->wf, seed, l, LLMRS_T_V, H, r * kd, kd, 0, H, L.qkv.w, L.qkv.s, L.qkv.st, 1,
+                              qd + kd));
+        // o_proj: all rows, the input columns of this rank's heads
+        LLMRS_TRY(synth_quant(s, m->wf, seed, l, LLMRS_T_O, QD, 0, H, r * qd, qd, L.o.w, L.o.s, L.o.st, 1, 0));
+        // gate/up interleaved: device row 2i = gate i, 2i+1 = up i (this rank's FFN rows)
+        LLMRS_TRY(synth_quant(s, m->wf, seed, l, LLMRS_T_GATE, H, r * F, F, 0, H, L.gate_up.w, L.gate_up.s,
+                              L.gate_up.st, 2, 0));
+        LLMRS_TRY(synth_quant(s, m->wf, seed, l, LLMRS_T_UP, H, r * F, F, 0, H, L.gate_up.w, L.gate_up.s,
+                              L.gate_up.st, 2, 1));
+        // down_proj: all rows, this rank's FFN columns
+        LLMRS_TRY(synth_quant(s, m->wf, seed, l, LLMRS_T_DOWN, FF, 0, H, r * F, F, L.down.w, L.down.s, L.down.st, 1,
+                              0));
         LLMRS_TRY(synth_normal(s, seed, l, LLMRS_T_ATTN_NORM, H, 1.0f, 0.02f, L.attn_norm));
         LLMRS_TRY(synth_normal(s, seed, l, LLMRS_T_MLP_NORM, H, 1.0f, 0.02f, L.mlp_norm));
     }
     LLMRS_TRY(synth_normal(s, seed, LLMRS_GLOBAL_LAYER, LLMRS_T_EMBED, (size_t)V * H, 1.0f, 0.02f, m->embed));
     LLMRS_TRY(synth_normal(s, seed, LLMRS_GLOBAL_LAYER, LLMRS_T_FINAL_NORM, H, 1.0f, 0.02f, m->final_norm));
     if (m->cfg.tied_embeddings)
-        LLMRS_TRY(op_quantize_q4(s, m->embed, (size_t)V * H, m->lm_head.w, (float *)m->lm_head.s));
+        LLMRS_TRY(op_quantize_q4(s, m->embed + (size_t)r * Vl * H, (size_t)Vl * H, m->lm_head.w,
+                                 (float *)m->lm_head.s));
     else
-        LLMRS_TRY(synth_quant(s, m->wf, seed, LLMRS_GLOBAL_LAYER, LLMRS_T_LM_HEAD, H, 0, V, 0, H, m->lm_head.w,
+        LLMRS_TRY(synth_quant(s, m->wf, seed, LLMRS_GLOBAL_LAYER, LLMRS_T_LM_HEAD, H, r * Vl, Vl, 0, H, m->lm_head.w,
                               m->lm_head.s, m->lm_head.st, 1, 0));
     return finish_sync(m);
 }
@@ -729,6 +774,8 @@ static int upload_quant(llmrs_model *m, const QW &q, const void *h_codes, const 
 int llmrs_model_set_weight(llmrs_model *m, int layer, int which, const void *h_codes, const float *h_scales)
 {
     LLMRS_CHECK_ARG(m && h_codes, "NULL argument");
+    if (m->T > 1)
+        return fail(LLMRS_ENOTSUP, "set_weight: tensor-parallel models are filled by init_synthetic");
     cudaSetDevice(m->ctx->device);
     cudaStream_t s = m->ctx->stream;
     const int D = m->D, H = m->H, F = m->F, V = m->V;
@@ -814,7 +861,8 @@ int llmrs_kv_fill_synthetic(llmrs_model *m, uint64_t seed, int n_pos)
         return LLMRS_OK;
     cudaSetDevice(m->ctx->device);
     for (int l = 0; l < m->cfg.n_layers; l++)
-        LLMRS_TRY(synth_kv(m->ctx->stream, seed, l, 0, m->Hkv, n_pos, m->S, m->D, m->layers[l].kc, m->layers[l].vc));
+        LLMRS_TRY(synth_kv(m->ctx->stream, seed, l, m->rank * m->Hkv, m->Hkv, n_pos, m->S, m->D, m->layers[l].kc,
+                           m->layers[l].vc));
     return finish_sync(m);
 }
 
@@ -839,64 +887,6 @@ struct KernelTimer {
     }
 };
 
-// Bytes per CTA that a decode-step kernel prefetches into L2 for the next
-// kernel (LLMRS_L2_PREFETCH_KB; default 0 = off: on B200 the next kernel's
-// latency is set by its dependency wait and prologue, not by its first HBM
-// bytes, so the prefetch only adds traffic).
-static size_t l2_prefetch_cap(void)
-{
-    static const size_t cap = [] {
-        const char *e = getenv("LLMRS_L2_PREFETCH_KB");
-        const long v = e ? atol(e) : 0;
-        return (size_t)(v < 0 ? 0 : v) * 1024;
-    }();
-    return cap;
-}
-
-// next kernel is the GEMV over q: each of its CTAs gets its first rows
-static NextPrefetch prefetch_rows(const QW &q)
-{
-    NextPrefetch pf;
-    const size_t cap = l2_prefetch_cap();
-    if (!q.plan.fast || cap == 0)
-        return pf;
-    const size_t wrow = q.plan.wf == 0 ? (size_t)q.k / 2 : (size_t)q.k;
-    const size_t srow = (size_t)(q.k / 32) * (q.plan.st == LLMRS_F16 ? 2 : 4);
-    const size_t rpc = (size_t)q.plan.rows_per_cta;
-    size_t rows = cap / (wrow + srow);
-    rows = rows < rpc ? rows : rpc;
-    pf.kind = PF_ROWS;
-    pf.ncta = q.plan.grid;
-    pf.a = q.w;
-    pf.a_stride = rpc * wrow;
-    pf.a_bytes = rows * wrow;
-    pf.a_end = (size_t)q.n * wrow;
-    pf.b = reinterpret_cast<const uint8_t *>(q.s);
-    pf.b_stride = rpc * srow;
-    pf.b_bytes = rows * srow;
-    pf.b_end = (size_t)q.n * srow;
-    return pf;
-}
-
-// next kernel is decode attention over layer L's cache
-static NextPrefetch prefetch_kv(const llmrs_model *m, const LayerW &L)
-{
-    NextPrefetch pf;
-    const size_t cap = l2_prefetch_cap();
-    if (cap == 0)
-        return pf;
-    pf.kind = PF_KV;
-    pf.ncta = m->n_splits * m->Hkv;
-    pf.kc = L.kc;
-    pf.vc = L.vc;
-    pf.state = m->state;
-    pf.max_seq = m->S;
-    pf.head_dim = m->D;
-    pf.n_splits = m->n_splits;
-    pf.kv_bytes = cap / 2;
-    return pf;
-}
-
 static int enqueue_step(llmrs_model *m, cudaStream_t s, KernelTimer *kt = nullptr, unsigned long long *trace = nullptr)
 {
     int slot = 0;
@@ -907,6 +897,23 @@ static int enqueue_step(llmrs_model *m, cudaStream_t s, KernelTimer *kt = nullpt
     const int H = m->H, F = m->F;
     const int qkv_rows = (m->Hq + 2 * m->Hkv) * m->D;
     uint32_t *err = &m->state->err;
+    // Tensor parallel: o_proj and down_proj write partial sums to every rank
+    // (EPI_PARTIAL); the next GEMV's prologue waits for all of them and forms
+    // x = sum + x (PRO_AR_NORM).  The residual stream alternates between x
+    // (after down_proj) and x1 (after o_proj) so no CTA overwrites the value
+    // another CTA still reads.
+    const bool tp = m->T > 1;
+    const int L_n = m->cfg.n_layers;
+    auto ar_in = [&](GemvParams &g, int kind, int index, const QW &producer, const float *x_in, float *x_out) {
+        g.tp = m->d_tp;
+        g.state = m->state;
+        g.ar_kind = kind;
+        g.ar_index = index;
+        g.ar_per_step = L_n;
+        g.ar_arrivals = m->T * gemv_grid(producer.plan);
+        g.x = x_in;
+        g.x_out = x_out;
+    };
     for (int l = 0; l < m->cfg.n_layers; l++) {
         LayerW &L = m->layers[l];
         GemvParams p{};
@@ -929,8 +936,10 @@ static int enqueue_step(llmrs_model *m, cudaStream_t s, KernelTimer *kt = nullpt
             p.embed = m->embed;
             p.vocab = m->V;
             p.x_out = m->x;
+        } else if (tp) {
+            pro = PRO_AR_NORM;
+            ar_in(p, TP_CNT_DOWN, l - 1, m->layers[l - 1].down, m->x1, m->x);
         }
-        p.pf = prefetch_kv(m, L);
         LLMRS_TRY(mark(0));
         LLMRS_TRY(gemv_launch(L.qkv.plan, p, pro, EPI_STORE, s, overlap && l != 0));
         LLMRS_TRY(mark(-1));
@@ -954,7 +963,6 @@ static int enqueue_step(llmrs_model *m, cudaStream_t s, KernelTimer *kt = nullpt
         a.inv_sqrt_d = 1.0f / sqrtf((float)m->D);
         a.trace = trace;
         a.trace_slot = slot++;
-        a.pf = prefetch_rows(L.o);
         LLMRS_TRY(mark(1));
         LLMRS_TRY(attention_decode_launch(a, s, overlap));
         LLMRS_TRY(mark(-1));
@@ -970,9 +978,12 @@ static int enqueue_step(llmrs_model *m, cudaStream_t s, KernelTimer *kt = nullpt
         o.residual = m->x;
         o.trace = trace;
         o.trace_slot = slot++;
-        o.pf = prefetch_rows(L.gate_up);
+        if (tp) {
+            o.tp = m->d_tp;
+            o.ar_kind = TP_CNT_O;
+        }
         LLMRS_TRY(mark(2));
-        LLMRS_TRY(gemv_launch(L.o.plan, o, PRO_F32, EPI_RESIDUAL, s, overlap));
+        LLMRS_TRY(gemv_launch(L.o.plan, o, PRO_F32, tp ? EPI_PARTIAL : EPI_RESIDUAL, s, overlap));
         LLMRS_TRY(mark(-1));
         // (4) post RMSNorm + gate_up + SiLU*up (src/core/layer.rs:37-89)
         GemvParams g{};
@@ -987,9 +998,10 @@ static int enqueue_step(llmrs_model *m, cudaStream_t s, KernelTimer *kt = nullpt
         g.y = m->act;
         g.trace = trace;
         g.trace_slot = slot++;
-        g.pf = prefetch_rows(L.down);
+        if (tp)
+            ar_in(g, TP_CNT_O, l, L.o, m->x, m->x1);
         LLMRS_TRY(mark(3));
-        LLMRS_TRY(gemv_launch(L.gate_up.plan, g, PRO_NORM, EPI_SILU, s, overlap));
+        LLMRS_TRY(gemv_launch(L.gate_up.plan, g, tp ? PRO_AR_NORM : PRO_NORM, EPI_SILU, s, overlap));
         LLMRS_TRY(mark(-1));
         // (5) down + residual (src/core/layer.rs:96, 403)
         GemvParams d{};
@@ -1003,9 +1015,12 @@ static int enqueue_step(llmrs_model *m, cudaStream_t s, KernelTimer *kt = nullpt
         d.residual = m->x;
         d.trace = trace;
         d.trace_slot = slot++;
-        d.pf = l + 1 < m->cfg.n_layers ? prefetch_rows(m->layers[l + 1].qkv) : prefetch_rows(m->lm_head);
+        if (tp) {
+            d.tp = m->d_tp;
+            d.ar_kind = TP_CNT_DOWN;
+        }
         LLMRS_TRY(mark(4));
-        LLMRS_TRY(gemv_launch(L.down.plan, d, PRO_F32, EPI_RESIDUAL, s, overlap));
+        LLMRS_TRY(gemv_launch(L.down.plan, d, PRO_F32, tp ? EPI_PARTIAL : EPI_RESIDUAL, s, overlap));
         LLMRS_TRY(mark(-1));
     }
     // final RMSNorm + LM head + greedy argmax (src/core/model.rs:39-47, src/main.rs:185-190)
@@ -1014,7 +1029,7 @@ static int enqueue_step(llmrs_model *m, cudaStream_t s, KernelTimer *kt = nullpt
     h.eps = m->cfg.rms_eps;
     h.w = m->lm_head.w;
     h.scales = m->lm_head.s;
-    h.N = m->V;
+    h.N = m->Vl;
     h.K = H;
     h.x = m->x;
     h.norm_w = m->final_norm;
@@ -1023,9 +1038,14 @@ static int enqueue_step(llmrs_model *m, cudaStream_t s, KernelTimer *kt = nullpt
     h.token_log = m->token_log;
     h.trace = trace;
     h.trace_slot = slot++;
-    h.pf = prefetch_rows(m->layers[0].qkv); // the next step's first kernel
+    int hpro = PRO_NORM;
+    if (tp) {
+        hpro = PRO_AR_NORM;
+        ar_in(h, TP_CNT_DOWN, L_n - 1, m->layers[L_n - 1].down, m->x1, m->x);
+        h.row_offset = m->rank * m->Vl;
+    }
     LLMRS_TRY(mark(5));
-    LLMRS_TRY(gemv_launch(m->lm_head.plan, h, PRO_NORM, EPI_ARGMAX, s, overlap));
+    LLMRS_TRY(gemv_launch(m->lm_head.plan, h, hpro, EPI_ARGMAX, s, overlap));
     LLMRS_TRY(mark(-1));
     return LLMRS_OK;
 }
@@ -1055,6 +1075,9 @@ static int capture_step(llmrs_model *m, cudaGraphExec_t *out, unsigned long long
 
 static int ensure_graph(llmrs_model *m)
 {
+    if (m->T > 1 && !m->tp_connected)
+        return fail(LLMRS_EINVAL, "tensor-parallel model (rank %d of %d) is not connected to its peers", m->rank,
+                    m->T);
     if (m->graph)
         return LLMRS_OK;
     return capture_step(m, &m->graph, nullptr);
@@ -1096,7 +1119,7 @@ int llmrs_decode_step(llmrs_model *m, int token, int pos, float *h_logits, int *
     LLMRS_CUDA_TRY(cudaMemcpyAsync(out, &m->state->token, sizeof(int), cudaMemcpyDeviceToHost, s));
     LLMRS_CUDA_TRY(cudaMemcpyAsync(out + 1, &m->state->err, sizeof(int), cudaMemcpyDeviceToHost, s));
     if (h_logits)
-        LLMRS_CUDA_TRY(cudaMemcpyAsync(h_logits, m->logits, (size_t)m->V * 4, cudaMemcpyDeviceToHost, s));
+        LLMRS_CUDA_TRY(cudaMemcpyAsync(h_logits, m->logits, (size_t)m->Vl * 4, cudaMemcpyDeviceToHost, s));
     LLMRS_CUDA_TRY(cudaStreamSynchronize(s));
     LLMRS_TRY(check_state_err(m, (uint32_t)out[1]));
     if (h_argmax)
@@ -1149,7 +1172,7 @@ int llmrs_prefill(llmrs_model *m, const int *h_ids, int n, int start_pos, float 
     LLMRS_CUDA_TRY(cudaMemcpyAsync(out, &m->state->token, sizeof(int), cudaMemcpyDeviceToHost, s));
     LLMRS_CUDA_TRY(cudaMemcpyAsync(out + 1, &m->state->err, sizeof(int), cudaMemcpyDeviceToHost, s));
     if (h_logits)
-        LLMRS_CUDA_TRY(cudaMemcpyAsync(h_logits, m->logits, (size_t)m->V * 4, cudaMemcpyDeviceToHost, s));
+        LLMRS_CUDA_TRY(cudaMemcpyAsync(h_logits, m->logits, (size_t)m->Vl * 4, cudaMemcpyDeviceToHost, s));
     LLMRS_CUDA_TRY(cudaStreamSynchronize(s));
     LLMRS_TRY(check_state_err(m, (uint32_t)out[1]));
     if (h_argmax)
@@ -1161,7 +1184,7 @@ int llmrs_model_logits(llmrs_model *m, float *h_logits)
 {
     LLMRS_CHECK_ARG(m && h_logits, "NULL argument");
     cudaSetDevice(m->ctx->device);
-    LLMRS_CUDA_TRY(cudaMemcpyAsync(h_logits, m->logits, (size_t)m->V * 4, cudaMemcpyDeviceToHost, m->ctx->stream));
+    LLMRS_CUDA_TRY(cudaMemcpyAsync(h_logits, m->logits, (size_t)m->Vl * 4, cudaMemcpyDeviceToHost, m->ctx->stream));
     return finish_sync(m);
 }
 
@@ -1176,6 +1199,7 @@ int llmrs_model_profile_decode(llmrs_model *m, int token, int pos, float *ms_out
 {
     LLMRS_CHECK_ARG(m && ms_out && kind_out && n && *n > 0, "bad arguments");
     LLMRS_CHECK_ARG(token >= 0 && token < m->V && pos >= 0 && pos < m->S, "token/position out of range");
+    LLMRS_CHECK_ARG(m->T == 1 || m->tp_connected, "tensor-parallel model is not connected to its peers");
     cudaSetDevice(m->ctx->device);
     cudaStream_t s = m->ctx->stream;
     KernelTimer kt;
@@ -1207,6 +1231,8 @@ int llmrs_model_profile_decode(llmrs_model *m, int token, int pos, float *ms_out
 
 int llmrs_model_trace_decode(llmrs_model *m, int token, int pos, unsigned long long *h_marks, int *kinds, int *n)
 {
+    LLMRS_CHECK_ARG(m, "model is NULL");
+    LLMRS_CHECK_ARG(m->T == 1 || m->tp_connected, "tensor-parallel model is not connected to its peers");
     LLMRS_CHECK_ARG(m && h_marks && kinds && n, "NULL argument");
     LLMRS_CHECK_ARG(token >= 0 && token < m->V && pos >= 0 && pos < m->S, "token/position out of range");
     const int nk = m->kernels_per_step;
@@ -1262,6 +1288,67 @@ int llmrs_model_time_decode(llmrs_model *m, int token, int pos, int iters, float
     int *out = m->h_stage + 60;
     LLMRS_CUDA_TRY(cudaMemcpy(out + 1, &m->state->err, sizeof(int), cudaMemcpyDeviceToHost));
     return check_state_err(m, (uint32_t)out[1]);
+}
+
+// ------------------------------------------------------------ tensor parallel
+int llmrs_model_tp_region(llmrs_model *m, void **d_region, size_t *bytes)
+{
+    LLMRS_CHECK_ARG(m && d_region && bytes, "NULL argument");
+    LLMRS_CHECK_ARG(m->T > 1, "model is not tensor parallel (tp_size 1)");
+    *d_region = m->tp_region;
+    *bytes = m->tp_bytes;
+    return LLMRS_OK;
+}
+
+int llmrs_model_tp_connect(llmrs_model *m, void *const *regions)
+{
+    LLMRS_CHECK_ARG(m && regions, "NULL argument");
+    LLMRS_CHECK_ARG(m->T > 1, "model is not tensor parallel (tp_size 1)");
+    LLMRS_CHECK_ARG(regions[m->rank] == m->tp_region, "regions[%d] must be this rank's own region", m->rank);
+    TpLink h{};
+    h.rank = m->rank;
+    h.size = m->T;
+    for (int q = 0; q < m->T; q++) {
+        LLMRS_CHECK_ARG(regions[q] != nullptr, "region of rank %d is NULL", q);
+        uint8_t *b = reinterpret_cast<uint8_t *>(regions[q]);
+        h.ar[TP_CNT_O][q] = reinterpret_cast<float *>(b + m->tp_off_o);
+        h.ar[TP_CNT_DOWN][q] = reinterpret_cast<float *>(b + m->tp_off_d);
+        h.keys[q] = reinterpret_cast<unsigned long long *>(b + m->tp_off_keys);
+        h.cnt[q] = reinterpret_cast<unsigned long long *>(b + m->tp_off_cnt);
+    }
+    cudaSetDevice(m->ctx->device);
+    LLMRS_CUDA_TRY(cudaMemcpyAsync(m->d_tp, &h, sizeof(h), cudaMemcpyHostToDevice, m->ctx->stream));
+    LLMRS_TRY(finish_sync(m));
+    m->tp_connected = true;
+    return LLMRS_OK;
+}
+
+int llmrs_ipc_get_handle(const void *d_ptr, void *handle_out)
+{
+    LLMRS_CHECK_ARG(d_ptr && handle_out, "NULL argument");
+    static_assert(sizeof(cudaIpcMemHandle_t) == LLMRS_IPC_HANDLE_BYTES, "IPC handle size");
+    cudaIpcMemHandle_t h;
+    LLMRS_CUDA_TRY(cudaIpcGetMemHandle(&h, const_cast<void *>(d_ptr)));
+    memcpy(handle_out, &h, sizeof(h));
+    return LLMRS_OK;
+}
+
+int llmrs_ipc_open_handle(int device, const void *handle, void **d_ptr_out)
+{
+    LLMRS_CHECK_ARG(handle && d_ptr_out, "NULL argument");
+    LLMRS_CUDA_TRY(cudaSetDevice(device));
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle, sizeof(h));
+    LLMRS_CUDA_TRY(cudaIpcOpenMemHandle(d_ptr_out, h, cudaIpcMemLazyEnablePeerAccess));
+    return LLMRS_OK;
+}
+
+int llmrs_ipc_close_handle(int device, void *d_ptr)
+{
+    LLMRS_CHECK_ARG(d_ptr, "NULL argument");
+    LLMRS_CUDA_TRY(cudaSetDevice(device));
+    LLMRS_CUDA_TRY(cudaIpcCloseMemHandle(d_ptr));
+    return LLMRS_OK;
 }
 
 } // extern "C"

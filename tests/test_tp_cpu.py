@@ -1,0 +1,44 @@
+"""The N > 1 path on CPU: two gloo ranks (tests/tp_cpu_worker.py) check the
+IPC-handle exchange helper and that the tensor-parallel partition of the model
+-- the one the CUDA path implements -- reproduces the unsharded oracle (logits
+to rounding, greedy tokens identical)."""
+import json
+import os
+import socket
+import subprocess
+import sys
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def test_tensor_parallel_partition_two_gloo_ranks(orc):
+    cfg = dict(n_layers=2, hidden=256, n_heads=8, n_kv_heads=2, head_dim=32, ffn=512, vocab=1000, max_seq=16,
+               rms_eps=1e-5, rope_theta=500000.0, weight_format=0, tied_embeddings=1)
+    seed = 31
+    om = orc.Model(cfg)
+    om.init_synthetic(seed)
+    tokens = [orc.synth_token(seed, i, cfg["vocab"]) for i in range(4)]
+    ref = [om.forward([t], i) for i, t in enumerate(tokens)]
+    spec = dict(cfg=cfg, seed=seed, tokens=tokens)
+    env = dict(os.environ, CUDA_VISIBLE_DEVICES="")
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2",
+           "--master-addr", "127.0.0.1", "--master-port", str(free_port()),
+           os.path.join(ROOT, "tests", "tp_cpu_worker.py"), json.dumps(spec)]
+    r = subprocess.run(cmd, capture_output=True, text=True, timeout=300, env=env)
+    assert r.returncode == 0, r.stderr[-4000:]
+    line = [ln for ln in r.stdout.splitlines() if ln.startswith("TPCPU ")]
+    assert line, r.stdout[-2000:]
+    got = json.loads(line[0][len("TPCPU "):])
+    for g, o in zip(got, ref):
+        g = np.asarray(g, np.float32)
+        assert orc.argmax(g) == orc.argmax(o)
+        rel = float(np.linalg.norm((g - o).astype(np.float64)) / np.linalg.norm(o.astype(np.float64)))
+        assert rel < 1e-3, rel
