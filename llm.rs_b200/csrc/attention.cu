@@ -24,6 +24,7 @@
 #include <mutex>
 
 #include "attention.cuh"
+#include "attention_core.cuh"
 #include "common.cuh"
 
 namespace llmrs {
@@ -51,17 +52,6 @@ struct AttnWarps {
     static constexpr int value = D >= 128 ? 12 : 16;
 };
 
-// K chunk in shared memory: the 3-D box [D/32 segments][CH rows][32 floats]
-// with the 128-byte swizzle (16-byte unit u of 128-byte line L lands at unit
-// u ^ (L % 8)), so lanes reading the same columns of 8 different rows hit 8
-// different bank groups.  Float index of (row r, column d):
-template <int CHR>
-__device__ __forceinline__ int kswz(int r, int d)
-{
-    const int line = (d >> 5) * CHR + r;
-    return line * 32 + ((((d >> 2) & 7) ^ (line & 7)) << 2) + (d & 3);
-}
-
 template <int D, int NREP>
 struct AttnLayout {
     static constexpr int NW = AttnWarps<D>::value;
@@ -83,75 +73,6 @@ struct AttnLayout {
     static_assert(KBYTES % 1024 == 0 && CH == 8, "swizzled K boxes must stay 1024-byte aligned");
 };
 
-// v[j] holds lane-partial sums of 32 dot products; on return lane i holds the
-// full sum of dot product i.
-__device__ __forceinline__ float butterfly32(float (&v)[32], int lane)
-{
-#pragma unroll
-    for (int w = 16; w >= 1; w >>= 1) {
-        const bool upper = (lane & w) != 0;
-#pragma unroll
-        for (int j = 0; j < w; j++) {
-            const float send = upper ? v[j] : v[j + w];
-            const float keep = upper ? v[j + w] : v[j];
-            v[j] = keep + __shfl_xor_sync(0xffffffffu, send, w);
-        }
-    }
-    return v[0];
-}
-
-// cos/sin table values this lane needs for rotate-half RoPE (lane l holds
-// dims l*DL.., frequency index (l % 16)*DL + k)
-template <int D>
-__device__ __forceinline__ void rope_table_lane(float (&c)[D / 32], float (&s)[D / 32], int lane, const float *cosr,
-                                                const float *sinr)
-{
-    constexpr int DL = D / 32;
-#pragma unroll
-    for (int k = 0; k < DL; k++) {
-        c[k] = cosr[(lane & 15) * DL + k];
-        s[k] = sinr[(lane & 15) * DL + k];
-    }
-}
-
-// rotate-half RoPE of one head held DL values per lane, exact reference
-// arithmetic: x[j]*cos - x[j+mid]*sin ; x[j]*sin + x[j+mid]*cos
-template <int D>
-__device__ __forceinline__ void rope_lane(float (&x)[D / 32], int lane, const float (&c)[D / 32],
-                                          const float (&s)[D / 32])
-{
-    constexpr int DL = D / 32;
-    float other[DL];
-#pragma unroll
-    for (int k = 0; k < DL; k++)
-        other[k] = __shfl_xor_sync(0xffffffffu, x[k], 16);
-    const bool upper = lane >= 16;
-#pragma unroll
-    for (int k = 0; k < DL; k++) {
-        if (!upper)
-            x[k] = __fsub_rn(__fmul_rn(x[k], c[k]), __fmul_rn(other[k], s[k]));
-        else
-            x[k] = __fadd_rn(__fmul_rn(other[k], s[k]), __fmul_rn(x[k], c[k]));
-    }
-}
-
-// DL consecutive floats of a shared-memory row (16- or 8-byte vector load)
-template <int DL>
-__device__ __forceinline__ void lds_lane(float (&r)[DL], const float *src)
-{
-    if constexpr (DL == 4) {
-        const float4 t = *reinterpret_cast<const float4 *>(src);
-        r[0] = t.x; r[1] = t.y; r[2] = t.z; r[3] = t.w;
-    } else if constexpr (DL == 2) {
-        const float2 t = *reinterpret_cast<const float2 *>(src);
-        r[0] = t.x; r[1] = t.y;
-    } else {
-#pragma unroll
-        for (int k = 0; k < DL; k++)
-            r[k] = src[k];
-    }
-}
-
 template <int D, int NREP>
 __global__ void __launch_bounds__(AttnWarps<D>::value * 32, 1) attn_decode_kernel(const __grid_constant__ AttnParams p)
 {
@@ -160,8 +81,6 @@ __global__ void __launch_bounds__(AttnWarps<D>::value * 32, 1) attn_decode_kerne
     constexpr int NW = Lay::NW;
     constexpr int NT = NW * 32;
     constexpr int DL = D / 32;
-    constexpr int G = 32 / NREP;   // positions per butterfly
-    constexpr int NFLY = CH / G;   // butterflies per chunk
     constexpr int ROWB = Lay::ROWB;
     extern __shared__ __align__(128) uint8_t smem_raw[];
     uint8_t *smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
@@ -279,94 +198,6 @@ __global__ void __launch_bounds__(AttnWarps<D>::value * 32, 1) attn_decode_kerne
         for (int k = 0; k < DL; k++)
             acc[h][k] = 0.0f;
 
-    // one chunk: positions 0..nvalid-1 of kt (K rows) / vt (V rows)
-    auto process = [&](const float *kt, const float *vt, int nvalid) {
-        // scores: lane owns (row b*G + lane/NREP, head lane%NREP) and sums
-        // q[d]*k[d] for d = 0..D-1 in order, unfused, like the reference's
-        // f32 dot (src/backend/cpu.rs:458-551, non-aarch64 branch), then
-        // scales by 1/sqrt(D) (src/core/layer.rs:258): bit-exact scores
-        float sc[NFLY];
-        {
-            const float *qh = q_s + (lane % NREP) * Lay::QS;
-            int roff[NFLY], rx[NFLY];
-            float dot[NFLY];
-#pragma unroll
-            for (int b = 0; b < NFLY; b++) {
-                const int r = b * G + lane / NREP;
-                roff[b] = r * 32;
-                rx[b] = r & 7;
-                dot[b] = 0.0f;
-            }
-#pragma unroll
-            for (int d4 = 0; d4 < D / 4; d4++) {
-                const float4 qv = *reinterpret_cast<const float4 *>(qh + d4 * 4);
-#pragma unroll
-                for (int b = 0; b < NFLY; b++) {
-                    const float4 kv = *reinterpret_cast<const float4 *>(
-                        kt + (d4 >> 3) * (CH * 32) + roff[b] + (((d4 & 7) ^ rx[b]) << 2));
-                    float t = dot[b];
-                    t = __fadd_rn(t, __fmul_rn(qv.x, kv.x));
-                    t = __fadd_rn(t, __fmul_rn(qv.y, kv.y));
-                    t = __fadd_rn(t, __fmul_rn(qv.z, kv.z));
-                    t = __fadd_rn(t, __fmul_rn(qv.w, kv.w));
-                    dot[b] = t;
-                }
-            }
-#pragma unroll
-            for (int b = 0; b < NFLY; b++)
-                sc[b] = (b * G + lane / NREP) < nvalid ? __fmul_rn(dot[b], p.inv_sqrt_d) : -INFINITY;
-        }
-        // lane holds (position b*G + lane/NREP, head lane%NREP) for each b
-        float tmax = sc[0];
-#pragma unroll
-        for (int b = 1; b < NFLY; b++)
-            tmax = fmaxf(tmax, sc[b]);
-#pragma unroll
-        for (int o = NREP; o < 32; o <<= 1)
-            tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, o));
-        const float m_new = fmaxf(m_run, tmax);
-        const float corr = (m_run == -INFINITY) ? 0.0f : expf(m_run - m_new);
-        float psum = 0.0f;
-#pragma unroll
-        for (int b = 0; b < NFLY; b++) {
-            const float pr = (sc[b] == -INFINITY) ? 0.0f : expf(sc[b] - m_new);
-            probs[b * 32 + lane] = pr; // index position * NREP + head
-            psum += pr;
-        }
-#pragma unroll
-        for (int o = NREP; o < 32; o <<= 1)
-            psum += __shfl_xor_sync(0xffffffffu, psum, o);
-        l_run = l_run * corr + psum;
-        m_run = m_new;
-#pragma unroll
-        for (int h = 0; h < NREP; h++) {
-            const float ch = __shfl_sync(0xffffffffu, corr, h);
-#pragma unroll
-            for (int k = 0; k < DL; k++)
-                acc[h][k] *= ch;
-        }
-        __syncwarp();
-#pragma unroll
-        for (int pl = 0; pl < CH; pl++) {
-            if (pl < nvalid) {
-                float vr[DL];
-                lds_lane<DL>(vr, vt + pl * D + lane * DL);
-                float ph[NREP];
-#pragma unroll
-                for (int h4 = 0; h4 < NREP; h4 += 4) {
-                    const float4 t = *reinterpret_cast<const float4 *>(probs + pl * NREP + h4);
-                    ph[h4] = t.x; ph[h4 + 1] = t.y; ph[h4 + 2] = t.z; ph[h4 + 3] = t.w;
-                }
-#pragma unroll
-                for (int h = 0; h < NREP; h++)
-#pragma unroll
-                    for (int k = 0; k < DL; k++)
-                        acc[h][k] = fmaf(ph[h], vr[k], acc[h][k]);
-            }
-        }
-        __syncwarp();
-    };
-
     bool ok = true;
     for (int j = 0; j < mine; j++) {
         const int slot = j & 1;
@@ -377,7 +208,8 @@ __global__ void __launch_bounds__(AttnWarps<D>::value * 32, 1) attn_decode_kerne
         if (ok) {
             const int rows = min(CH, t1 - (t0 + (warp + j * NW) * CH));
             const float *st = reinterpret_cast<const float *>(ring + slot * Lay::SLOT);
-            process(st, st + Lay::KBYTES / 4, rows);
+            attn_chunk<D, NREP, CH>(st, 0, st + Lay::KBYTES / 4, rows, q_s, Lay::QS, probs, p.inv_sqrt_d, m_run,
+                                    l_run, acc, lane);
         }
         if (ok && lane == 0 && j + 2 < mine) {
             fence_proxy_async_smem(); // this warp's reads of the slot precede the refill
@@ -387,15 +219,16 @@ __global__ void __launch_bounds__(AttnWarps<D>::value * 32, 1) attn_decode_kerne
     LLMRS_ATTN_MARK(3);
     LLMRS_ATTN_MARK_MAX(7);
     if (appender && pos_ok) {
-        // the new position, staged in this warp's (now idle) first slot
+        // the new position, staged as plain rows in this warp's (now idle) first slot
         float *st = reinterpret_cast<float *>(ring);
 #pragma unroll
         for (int k = 0; k < DL; k++) {
-            st[kswz<CH>(0, lane * DL + k)] = kk[k];
-            st[Lay::KBYTES / 4 + lane * DL + k] = vv[k];
+            st[lane * DL + k] = kk[k];
+            st[D + lane * DL + k] = vv[k];
         }
         __syncwarp();
-        process(st, st + Lay::KBYTES / 4, 1);
+        attn_new_position<D, NREP>(st, st + D, q_s, Lay::QS, p.inv_sqrt_d, m_run, l_run, acc, lane);
+        __syncwarp();
     }
 
     // merge the warps of this CTA: warp partials at the start of each ring
