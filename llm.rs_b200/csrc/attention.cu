@@ -335,9 +335,11 @@ __global__ void __launch_bounds__(AttnWarps<D>::value * 32, 1) attn_decode_kerne
     LLMRS_ATTN_MARK(6);
 }
 
+} // namespace
+
 // K cache [n_kv * max_seq rows][D] viewed as (x: 32 floats of a 128-byte
-// segment, y: row, z: segment), boxes of CH rows x every segment, swizzled
-int encode_k_map(CUtensorMap *map, const float *kc, int rows, int D)
+// segment, y: row, z: segment), boxes of box_rows rows x every segment, swizzled
+int encode_k_map(CUtensorMap *map, const float *kc, int rows, int D, int box_rows)
 {
     auto fn = tensor_map_encoder();
     if (!fn)
@@ -345,7 +347,7 @@ int encode_k_map(CUtensorMap *map, const float *kc, int rows, int D)
     LLMRS_CHECK_ARG(((uintptr_t)kc & 15) == 0, "attention: K cache not 16-byte aligned");
     cuuint64_t dims[3] = {32, (cuuint64_t)rows, (cuuint64_t)(D / 32)};
     cuuint64_t strides[2] = {(cuuint64_t)D * 4, 128};
-    cuuint32_t box[3] = {32, (cuuint32_t)CH, (cuuint32_t)(D / 32)};
+    cuuint32_t box[3] = {32, (cuuint32_t)box_rows, (cuuint32_t)(D / 32)};
     cuuint32_t estr[3] = {1, 1, 1};
     CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float *>(kc), dims, strides, box, estr,
                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -354,6 +356,8 @@ int encode_k_map(CUtensorMap *map, const float *kc, int rows, int D)
         return fail(LLMRS_ECUDA, "cuTensorMapEncodeTiled (K cache) failed (%d)", (int)r);
     return LLMRS_OK;
 }
+
+namespace {
 
 template <int D, int NREP>
 int launch_attn(const AttnParams &p, cudaStream_t stream, bool pdl)
@@ -409,7 +413,7 @@ int attention_decode_launch(const AttnParams &p, cudaStream_t stream, bool pdl)
     LLMRS_CHECK_ARG(((uintptr_t)p.vc & 15) == 0, "attention: V cache not 16-byte aligned");
     LLMRS_CHECK_ARG(p.n_splits >= 1 && p.n_splits <= 32, "attention: %d splits outside [1, 32]", p.n_splits);
     AttnParams q = p;
-    LLMRS_TRY(encode_k_map(&q.tk, p.kc, p.n_kv * p.max_seq, p.head_dim));
+    LLMRS_TRY(encode_k_map(&q.tk, p.kc, p.n_kv * p.max_seq, p.head_dim, CH));
     if (p.head_dim == 128 && nrep == 4)
         return launch_attn<128, 4>(q, stream, pdl);
     if (p.head_dim == 128 && nrep == 8)

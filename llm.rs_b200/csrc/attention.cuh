@@ -31,5 +31,7 @@ int attention_default_splits(int n_kv);
 // set kernel attributes on the current device (once per context, outside capture)
 int attention_prepare(void);
 size_t attention_partials_floats(int n_heads, int head_dim, int n_splits);
+// tensor map of a K cache [rows][D] as swizzled boxes of box_rows rows (see attention.cu)
+int encode_k_map(CUtensorMap *map, const float *kc, int rows, int D, int box_rows);
 
 } // namespace llmrs

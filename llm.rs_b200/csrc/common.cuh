@@ -51,6 +51,8 @@ enum : uint32_t {
     DEV_ERR_PEER_TIMEOUT = 2,
     DEV_ERR_BAD_TOKEN = 3,
     DEV_ERR_BAD_POS = 4,
+    DEV_ERR_BAD_OP = 5,       // decode-step kernel met an op it was not built for
+    DEV_ERR_STEP_TIMEOUT = 6, // decode-step kernel: an op's input never completed
 };
 
 // launch a kernel; with pdl=true it may begin before the previous kernel in the
@@ -127,6 +129,11 @@ __device__ __forceinline__ void mbar_arrive(uint64_t *bar)
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
 }
 
+__device__ __forceinline__ void mbar_arrive_n(uint64_t *bar, uint32_t n)
+{
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(n) : "memory");
+}
+
 __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity)
 {
     uint32_t ok;
@@ -184,6 +191,11 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint32
 {
     if (mbar_try_wait(bar, parity))
         return true;
+    if (err) { // after one timeout in this launch, later waits give up at once
+        const uint32_t e = *reinterpret_cast<volatile uint32_t *>(err);
+        if (e == DEV_ERR_MBAR_TIMEOUT || e == DEV_ERR_PEER_TIMEOUT || e == DEV_ERR_STEP_TIMEOUT)
+            return false;
+    }
     uint64_t t0 = globaltimer_ns();
     for (uint32_t it = 1;; ++it) {
         if (mbar_try_wait(bar, parity))

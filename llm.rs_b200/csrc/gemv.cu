@@ -92,7 +92,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         // activation (queued behind the weight stream it would arrive last).
         if (lane == 0) {
             uint32_t fill_par = 0, filled = 0;
-            gemv_produce<WF, ST>(&tw, &ts, p, w, sm, fill_par, filled, policy_evict_first(), min(p.n_pre, S));
+            InFlight q; // unbounded: one op per kernel, nothing else to wait behind it
+            gemv_produce<WF, ST>(&tw, &ts, p, w, sm, fill_par, filled, policy_evict_first(), min(p.n_pre, S), q);
             LLMRS_TRACE_FLUSH(1);
         }
         return;

@@ -238,7 +238,7 @@ __device__ __forceinline__ void quantize_block8(const float (&v)[4], int j, bool
 // (larger K) load as they go.
 
 template <int WF, int PRO>
-__device__ void load_activation(const GemvParams &p, uint32_t *act, float *act_s, int *act_c, float *red, int tid,
+__device__ __forceinline__ void load_activation(const GemvParams &p, uint32_t *act, float *act_s, int *act_c, float *red, int tid,
                                 int nthr, int bar, uint64_t *issued)
 {
     const int K = p.K, nb = K >> 5;
@@ -482,7 +482,7 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, i
 
 // Publish the step's greedy token: CTA max -> global atomicMax; the last CTA
 // writes the token, logs it and advances the decode position.
-__device__ void argmax_finalize(const GemvParams &p, unsigned long long key, int tid, int nthr, int bar)
+__device__ __forceinline__ void argmax_finalize(const GemvParams &p, unsigned long long key, int tid, int nthr, int bar)
 {
     __shared__ unsigned long long s_key[32];
     const int warp = tid >> 5, lane = tid & 31;
@@ -547,6 +547,7 @@ struct GemvSmem {
     float *act_s;            // activation block scales
     int *act_c;              // per block: -8 * sum(q) (Q4 offset)
     float *tbuf, *linkbuf, *red;
+    unsigned long long *ready_mark = nullptr; // optional: latest time a CTA finished the prologue
 };
 
 // This CTA's share of a GEMV: rows [r0, r1) in tiles of B rows.  TPS tile sets
@@ -610,13 +611,53 @@ __device__ __forceinline__ uint32_t gemv_link_parity(const GemvWork &w)
     return m;
 }
 
+// Bound on the stages a producer has requested that have not landed yet.  A
+// deep queue of bulk copies makes every other memory access of the SM (the
+// activation loads, epilogue stores, completion counters) wait behind it; a
+// few stages in flight (about the bandwidth-delay product of one SM) keep the
+// HBM busy without that.
+struct InFlight {
+    int cap = 0; // 0: unbounded
+    int n = 0, head = 0;
+    uint8_t st[8], seq[8]; // stage and fill number of each outstanding fill, oldest at head
+    uint8_t fills[8] = {}; // fills of each stage so far (mod 256)
+};
+
+// Before a new request: while `cap` are outstanding, wait for the oldest to
+// land.  An entry whose stage has been filled again since has landed (the
+// refill needed its consumption), so it is dropped without waiting.
+__device__ __forceinline__ bool inflight_admit(InFlight &q, uint64_t *full, uint32_t *err)
+{
+    while (q.cap > 0 && q.n >= q.cap) {
+        const int s = q.st[q.head];
+        if (q.fills[s] == (uint8_t)(q.seq[q.head] + 1) && !mbar_wait(&full[s], q.seq[q.head] & 1u, err))
+            return false;
+        q.head = (q.head + 1) & 7;
+        q.n--;
+    }
+    return true;
+}
+
+// after requesting a fill of stage s (its full barrier completes phase fills[s])
+__device__ __forceinline__ void inflight_push(InFlight &q, int s)
+{
+    if (q.cap > 0) {
+        const int t = (q.head + q.n) & 7;
+        q.st[t] = (uint8_t)s;
+        q.seq[t] = q.fills[s];
+        q.n++;
+    }
+    q.fills[s]++;
+}
+
 // Producer (one thread): stream this CTA's stages of one GEMV.  fill_par /
 // filled: per stage, parity of its fills so far / filled at least once (kept
 // across ops).  pre >= 0: after `pre` stages wait until the consumers have
 // requested the activation.  Returns false if a wait timed out.
 template <int WF, int ST>
-__device__ bool gemv_produce(const CUtensorMap *tw, const CUtensorMap *ts, const GemvParams &p, const GemvWork &w,
-                             const GemvSmem &sm, uint32_t &fill_par, uint32_t &filled, uint64_t pol, int pre)
+__device__ __forceinline__ bool gemv_produce(const CUtensorMap *tw, const CUtensorMap *ts, const GemvParams &p, const GemvWork &w,
+                             const GemvSmem &sm, uint32_t &fill_par, uint32_t &filled, uint64_t pol, int pre,
+                             InFlight &q)
 {
     constexpr int W_ROW = CB * wbytes_per_block(WF);
     constexpr int S_ROW = CB * sbytes(ST);
@@ -649,12 +690,15 @@ __device__ bool gemv_produce(const CUtensorMap *tw, const CUtensorMap *ts, const
             LLMRS_TRACE_BEGIN(0);
             if ((filled & bit) && !mbar_wait(&sm.empty[s], (fill_par & bit) ? 0u : 1u, p.err))
                 return false;
+            if (!inflight_admit(q, sm.full, p.err))
+                return false;
             LLMRS_TRACE_END(0);
             const int y = w.r0 + gt[g] * w.B, c = gc[g];
             uint8_t *st = sm.ring + (size_t)s * sm.stage_bytes;
             mbar_arrive_expect_tx(&sm.full[s], stage_tx);
             tma_load_2d(st, tw, c * (W_ROW / 4), y, &sm.full[s], pol);
             tma_load_2d(st + sm.scale_off, ts, c * CB, y, &sm.full[s], pol);
+            inflight_push(q, s);
             fill_par ^= bit;
             filled |= bit;
             gc[g] += w.GT;
@@ -673,7 +717,7 @@ __device__ bool gemv_produce(const CUtensorMap *tw, const CUtensorMap *ts, const
 // across ops; advanced to the op's end on return).  The caller has already
 // waited for the op's input.
 template <int WF, int ST, int PRO, int EPI>
-__device__ void gemv_consume(const GemvParams &p, const GemvWork &w, const GemvSmem &sm, uint32_t &cpar,
+__device__ __forceinline__ void gemv_consume(const GemvParams &p, const GemvWork &w, const GemvSmem &sm, uint32_t &cpar,
                              uint32_t &lpar, int ctid)
 {
     constexpr int W_ROW = CB * wbytes_per_block(WF);
@@ -683,8 +727,11 @@ __device__ void gemv_consume(const GemvParams &p, const GemvWork &w, const GemvS
     LLMRS_TRACE_BEGIN(2);
     load_activation<WF, PRO>(p, sm.act, sm.act_s, sm.act_c, sm.red, ctid, PRO_THREADS, 1, sm.issued);
     named_bar_sync(1, PRO_THREADS);
-    if (ctid == 0)
+    if (ctid == 0) {
         trace_ready(p.trace, p.trace_slot);
+        if (sm.ready_mark)
+            atomicMax(sm.ready_mark, (unsigned long long)globaltimer_ns());
+    }
     LLMRS_TRACE_END(2);
 
     // warp (grp, wq): group grp = warp / WPG takes its steps of its tile set;

@@ -12,12 +12,14 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <algorithm>
 #include <mutex>
 #include <vector>
 
 #include "attention.cuh"
 #include "common.cuh"
 #include "gemv.cuh"
+#include "step.cuh"
 #include "llmrs_synth.h"
 #include "ops.cuh"
 
@@ -149,6 +151,13 @@ struct llmrs_model {
     size_t tp_bytes = 0, tp_off_o = 0, tp_off_d = 0, tp_off_keys = 0, tp_off_cnt = 0;
     TpLink *d_tp = nullptr;
     bool tp_connected = false;
+    // the persistent decode-step kernel (op list in device memory)
+    bool step_tried = false;
+    void *step_buf = nullptr;
+    StepOp *step_ops = nullptr;
+    unsigned long long *step_done = nullptr;
+    int step_n_ops = 0, step_stages = 0, step_kmax = 0, step_grid = 0;
+    size_t step_smem = 0;
     unsigned int *att_counter = nullptr;
     StepState *state = nullptr;
     int *token_log = nullptr;
@@ -216,6 +225,8 @@ int llmrs_ctx_create(int device, llmrs_ctx **out)
     int rc = gemv_prepare();
     if (rc == LLMRS_OK)
         rc = attention_prepare();
+    if (rc == LLMRS_OK)
+        rc = step_prepare();
     if (rc != LLMRS_OK) {
         cudaFree(c->d_err);
         cudaStreamDestroy(c->own);
@@ -513,6 +524,8 @@ static void model_free(llmrs_model *m)
         cudaFree(m->arena.base);
     if (m->tp_region)
         cudaFree(m->tp_region);
+    if (m->step_buf)
+        cudaFree(m->step_buf);
     if (m->h_stage)
         cudaFreeHost(m->h_stage);
     delete m;
@@ -887,13 +900,27 @@ struct KernelTimer {
     }
 };
 
-static int enqueue_step(llmrs_model *m, cudaStream_t s, KernelTimer *kt = nullptr, unsigned long long *trace = nullptr)
+// One op of a decode step, as both execution paths see it: a GEMV over a
+// weight matrix (with its prologue / epilogue variant) or decode attention.
+// wait_op: the op whose whole output this op reads (-1: none, or an
+// all-reduce prologue that waits on the ranks' counters itself).
+struct HostOp {
+    int kind = OP_GEMV;
+    int trace_kind = 0; // KERNEL kind of profile_decode / trace_decode
+    const QW *q = nullptr;
+    GemvParams g{};
+    int pro = PRO_F32, epi = EPI_STORE;
+    AttnParams a{};
+    int wait_op = -1;
+};
+
+// The decode step (src/core/model.rs:17-49 for a 1-token chunk) as an op
+// list.  grid: CTAs every GEMV launches with when all ops run in one
+// persistent kernel (0: each GEMV's own plan grid).
+static void build_ops(llmrs_model *m, std::vector<HostOp> &ops, unsigned long long *trace, int grid)
 {
+    ops.clear();
     int slot = 0;
-    // with a timer every kernel is bracketed by events and launched without
-    // programmatic overlap, so each event pair times exactly one kernel
-    const bool overlap = kt == nullptr;
-    auto mark = [&](int kind) { return kt ? kt->mark(s, kind) : LLMRS_OK; };
     const int H = m->H, F = m->F;
     const int qkv_rows = (m->Hq + 2 * m->Hkv) * m->D;
     uint32_t *err = &m->state->err;
@@ -910,16 +937,29 @@ static int enqueue_step(llmrs_model *m, cudaStream_t s, KernelTimer *kt = nullpt
         g.ar_kind = kind;
         g.ar_index = index;
         g.ar_per_step = L_n;
-        g.ar_arrivals = m->T * gemv_grid(producer.plan);
+        g.ar_arrivals = m->T * (grid ? grid : gemv_grid(producer.plan));
         g.x = x_in;
         g.x_out = x_out;
     };
-    for (int l = 0; l < m->cfg.n_layers; l++) {
+    auto push_gemv = [&](int tkind, const QW &q, const GemvParams &g, int pro, int epi) {
+        HostOp o;
+        o.kind = OP_GEMV;
+        o.trace_kind = tkind;
+        o.q = &q;
+        o.g = g;
+        o.g.trace = trace;
+        o.g.trace_slot = slot++;
+        o.pro = pro;
+        o.epi = epi;
+        o.wait_op = (ops.empty() || pro == PRO_AR_NORM) ? -1 : (int)ops.size() - 1;
+        ops.push_back(o);
+    };
+    for (int l = 0; l < L_n; l++) {
         LayerW &L = m->layers[l];
+        // (1) input RMSNorm + Q8_0 + fused QKV projection (layer 0: embedding gather, src/main.rs:159-171)
         GemvParams p{};
         p.err = err;
         p.eps = m->cfg.rms_eps;
-        // (1) input RMSNorm + Q8_0 + fused QKV projection (layer 0: embedding gather, src/main.rs:159-171)
         p.w = L.qkv.w;
         p.scales = L.qkv.s;
         p.N = qkv_rows;
@@ -928,8 +968,6 @@ static int enqueue_step(llmrs_model *m, cudaStream_t s, KernelTimer *kt = nullpt
         p.norm_w = L.attn_norm;
         p.y = m->qkv;
         p.state = m->state;
-        p.trace = trace;
-        p.trace_slot = slot++;
         int pro = PRO_NORM;
         if (l == 0) {
             pro = PRO_EMBED_NORM;
@@ -940,11 +978,12 @@ static int enqueue_step(llmrs_model *m, cudaStream_t s, KernelTimer *kt = nullpt
             pro = PRO_AR_NORM;
             ar_in(p, TP_CNT_DOWN, l - 1, m->layers[l - 1].down, m->x1, m->x);
         }
-        LLMRS_TRY(mark(0));
-        LLMRS_TRY(gemv_launch(L.qkv.plan, p, pro, EPI_STORE, s, overlap && l != 0));
-        LLMRS_TRY(mark(-1));
+        push_gemv(0, L.qkv, p, pro, EPI_STORE);
         // (2) RoPE + KV append + attention (src/core/layer.rs:175-333)
-        AttnParams a{};
+        HostOp at;
+        at.kind = OP_ATTN;
+        at.trace_kind = 1;
+        AttnParams &a = at.a;
         a.qkv = m->qkv;
         a.kc = L.kc;
         a.vc = L.vc;
@@ -963,9 +1002,8 @@ static int enqueue_step(llmrs_model *m, cudaStream_t s, KernelTimer *kt = nullpt
         a.inv_sqrt_d = 1.0f / sqrtf((float)m->D);
         a.trace = trace;
         a.trace_slot = slot++;
-        LLMRS_TRY(mark(1));
-        LLMRS_TRY(attention_decode_launch(a, s, overlap));
-        LLMRS_TRY(mark(-1));
+        at.wait_op = (int)ops.size() - 1;
+        ops.push_back(at);
         // (3) o_proj + residual (src/core/layer.rs:332, 386)
         GemvParams o{};
         o.err = err;
@@ -976,15 +1014,11 @@ static int enqueue_step(llmrs_model *m, cudaStream_t s, KernelTimer *kt = nullpt
         o.x = m->ctxv;
         o.y = m->x;
         o.residual = m->x;
-        o.trace = trace;
-        o.trace_slot = slot++;
         if (tp) {
             o.tp = m->d_tp;
             o.ar_kind = TP_CNT_O;
         }
-        LLMRS_TRY(mark(2));
-        LLMRS_TRY(gemv_launch(L.o.plan, o, PRO_F32, tp ? EPI_PARTIAL : EPI_RESIDUAL, s, overlap));
-        LLMRS_TRY(mark(-1));
+        push_gemv(2, L.o, o, PRO_F32, tp ? EPI_PARTIAL : EPI_RESIDUAL);
         // (4) post RMSNorm + gate_up + SiLU*up (src/core/layer.rs:37-89)
         GemvParams g{};
         g.err = err;
@@ -996,13 +1030,9 @@ static int enqueue_step(llmrs_model *m, cudaStream_t s, KernelTimer *kt = nullpt
         g.x = m->x;
         g.norm_w = L.mlp_norm;
         g.y = m->act;
-        g.trace = trace;
-        g.trace_slot = slot++;
         if (tp)
             ar_in(g, TP_CNT_O, l, L.o, m->x, m->x1);
-        LLMRS_TRY(mark(3));
-        LLMRS_TRY(gemv_launch(L.gate_up.plan, g, tp ? PRO_AR_NORM : PRO_NORM, EPI_SILU, s, overlap));
-        LLMRS_TRY(mark(-1));
+        push_gemv(3, L.gate_up, g, tp ? PRO_AR_NORM : PRO_NORM, EPI_SILU);
         // (5) down + residual (src/core/layer.rs:96, 403)
         GemvParams d{};
         d.err = err;
@@ -1013,15 +1043,11 @@ static int enqueue_step(llmrs_model *m, cudaStream_t s, KernelTimer *kt = nullpt
         d.x = m->act;
         d.y = m->x;
         d.residual = m->x;
-        d.trace = trace;
-        d.trace_slot = slot++;
         if (tp) {
             d.tp = m->d_tp;
             d.ar_kind = TP_CNT_DOWN;
         }
-        LLMRS_TRY(mark(4));
-        LLMRS_TRY(gemv_launch(L.down.plan, d, PRO_F32, tp ? EPI_PARTIAL : EPI_RESIDUAL, s, overlap));
-        LLMRS_TRY(mark(-1));
+        push_gemv(4, L.down, d, PRO_F32, tp ? EPI_PARTIAL : EPI_RESIDUAL);
     }
     // final RMSNorm + LM head + greedy argmax (src/core/model.rs:39-47, src/main.rs:185-190)
     GemvParams h{};
@@ -1036,26 +1062,127 @@ static int enqueue_step(llmrs_model *m, cudaStream_t s, KernelTimer *kt = nullpt
     h.y = m->logits;
     h.state = m->state;
     h.token_log = m->token_log;
-    h.trace = trace;
-    h.trace_slot = slot++;
     int hpro = PRO_NORM;
     if (tp) {
         hpro = PRO_AR_NORM;
         ar_in(h, TP_CNT_DOWN, L_n - 1, m->layers[L_n - 1].down, m->x1, m->x);
         h.row_offset = m->rank * m->Vl;
     }
-    LLMRS_TRY(mark(5));
-    LLMRS_TRY(gemv_launch(m->lm_head.plan, h, hpro, EPI_ARGMAX, s, overlap));
-    LLMRS_TRY(mark(-1));
+    push_gemv(5, m->lm_head, h, hpro, EPI_ARGMAX);
+}
+
+// one kernel per op; every kernel but the step's first starts under
+// programmatic dependent launch
+static int enqueue_step(llmrs_model *m, cudaStream_t s, KernelTimer *kt = nullptr, unsigned long long *trace = nullptr)
+{
+    // with a timer every kernel is bracketed by events and launched without
+    // programmatic overlap, so each event pair times exactly one kernel
+    const bool overlap = kt == nullptr;
+    std::vector<HostOp> ops;
+    build_ops(m, ops, trace, 0);
+    for (size_t i = 0; i < ops.size(); i++) {
+        const HostOp &o = ops[i];
+        if (kt)
+            LLMRS_TRY(kt->mark(s, o.trace_kind));
+        if (o.kind == OP_GEMV)
+            LLMRS_TRY(gemv_launch(o.q->plan, o.g, o.pro, o.epi, s, overlap && i != 0));
+        else
+            LLMRS_TRY(attention_decode_launch(o.a, s, overlap));
+        if (kt)
+            LLMRS_TRY(kt->mark(s, -1));
+    }
     return LLMRS_OK;
+}
+
+// The persistent decode-step kernel: upload the op list once per model.
+static bool step_kernel_enabled(void)
+{
+    static const bool on = [] {
+        const char *e = getenv("LLMRS_STEP_KERNEL");
+        return e && e[0] == '1';
+    }();
+    return on;
+}
+
+static int setup_step_kernel(llmrs_model *m)
+{
+    if (m->step_tried)
+        return LLMRS_OK;
+    m->step_tried = true;
+    if (!step_kernel_enabled())
+        return LLMRS_OK;
+    const int kmax = std::max(std::max(m->H, m->F), m->Hq * m->D);
+    int stages = 0;
+    const size_t smem = step_smem_bytes(m->wf, m->st, m->lm_head.st, m->D, m->Hq / m->Hkv, m->T > 1, kmax, &stages);
+    if (smem == 0)
+        return LLMRS_OK; // no kernel built for this shape: one kernel per op
+    const int G = m->ctx->sms;
+    std::vector<HostOp> ops;
+    build_ops(m, ops, nullptr, G);
+    std::vector<StepOp> h(ops.size());
+    for (size_t i = 0; i < ops.size(); i++) {
+        StepOp &so = h[i];
+        memset(&so, 0, sizeof(so));
+        const HostOp &o = ops[i];
+        so.kind = o.kind;
+        so.wait_op = o.wait_op;
+        if (o.kind == OP_GEMV) {
+            const GemvPlan &pl = o.q->plan;
+            if (!pl.fast)
+                return LLMRS_OK; // a shape only the fallback GEMV handles: one kernel per op
+            so.tw = pl.tw;
+            so.ts = pl.ts;
+            so.g = o.g;
+            so.g.n_stages = stages;
+            so.g.n_pre = -1;
+            so.g.box_rows = pl.box_rows;
+            so.g.rows_per_cta = pl.rows_per_cta;
+            so.pro = o.pro;
+            so.epi = o.epi;
+            so.wf = pl.wf;
+            so.st = pl.st;
+            if (pl.grid > G)
+                return LLMRS_OK;
+        } else {
+            so.a = o.a;
+            LLMRS_TRY(encode_k_map(&so.a.tk, o.a.kc, o.a.n_kv * o.a.max_seq, o.a.head_dim, STEP_ATTN_ROWS));
+            if (o.a.n_splits * o.a.n_kv > G)
+                return LLMRS_OK;
+        }
+    }
+    const size_t bytes = h.size() * sizeof(StepOp) + (ops.size() + 1) * 8; // + the launch counter
+    void *buf = nullptr;
+    LLMRS_CUDA_TRY(cudaMalloc(&buf, bytes));
+    m->step_buf = buf;
+    m->step_ops = reinterpret_cast<StepOp *>(buf);
+    m->step_done = reinterpret_cast<unsigned long long *>(reinterpret_cast<uint8_t *>(buf) + h.size() * sizeof(StepOp));
+    cudaStream_t s = m->ctx->stream;
+    LLMRS_CUDA_TRY(cudaMemcpyAsync(m->step_ops, h.data(), h.size() * sizeof(StepOp), cudaMemcpyHostToDevice, s));
+    LLMRS_CUDA_TRY(cudaMemsetAsync(m->step_done, 0, (ops.size() + 1) * 8, s));
+    LLMRS_CUDA_TRY(cudaStreamSynchronize(s));
+    m->step_n_ops = (int)ops.size();
+    m->step_smem = smem;
+    m->step_stages = stages;
+    m->step_kmax = kmax;
+    m->step_grid = G;
+    return LLMRS_OK;
+}
+
+static int launch_step_kernel(llmrs_model *m, cudaStream_t s, unsigned long long *trace)
+{
+    return step_launch(m->wf, m->st, m->lm_head.st, m->D, m->Hq / m->Hkv, m->T > 1, m->step_kmax, m->step_stages,
+                       m->step_smem,
+                       m->step_grid, m->step_ops, m->step_n_ops, m->step_done, m->state, &m->state->err, trace, s);
 }
 
 static int capture_step(llmrs_model *m, cudaGraphExec_t *out, unsigned long long *trace)
 {
     cudaStream_t s = m->ctx->stream;
     cudaGraph_t g = nullptr;
+    LLMRS_TRY(setup_step_kernel(m));
+    const bool one_kernel = m->step_ops != nullptr;
     LLMRS_CUDA_TRY(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
-    int rc = enqueue_step(m, s, nullptr, trace);
+    int rc = one_kernel ? launch_step_kernel(m, s, trace) : enqueue_step(m, s, nullptr, trace);
     cudaError_t e = cudaStreamEndCapture(s, &g);
     if (rc != LLMRS_OK) {
         if (g)
@@ -1089,7 +1216,7 @@ static int check_state_err(llmrs_model *m, uint32_t e)
         return LLMRS_OK;
     cudaMemsetAsync(&m->state->err, 0, 4, m->ctx->stream);
     cudaStreamSynchronize(m->ctx->stream);
-    if (e == DEV_ERR_MBAR_TIMEOUT || e == DEV_ERR_PEER_TIMEOUT)
+    if (e == DEV_ERR_MBAR_TIMEOUT || e == DEV_ERR_PEER_TIMEOUT || e == DEV_ERR_STEP_TIMEOUT)
         return fail(LLMRS_ETIMEDOUT, "decode step: device wait timed out (code %u)", e);
     return fail(LLMRS_EDEVICE, "decode step: device error word %u (%s)", e,
                 e == DEV_ERR_BAD_TOKEN ? "token id out of range" : (e == DEV_ERR_BAD_POS ? "position out of range" : "?"));
