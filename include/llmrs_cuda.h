@@ -149,6 +149,17 @@ int llmrs_attention_decode_noalloc(void *cuda_stream, const float *d_qkv, float 
                                    const float *d_rope_cos, const float *d_rope_sin, float *d_out, int n_heads,
                                    int n_kv_heads, int head_dim, int max_seq, int pos, unsigned int *d_err);
 
+/* Fused causal attention for n_rows consecutive tokens at positions
+ * start_pos .. start_pos+n_rows-1 (the per-head loop of src/core/layer.rs:175-333
+ * for seq_len > 1, native GQA): RoPE of every row's q (in place in d_qkv) and k,
+ * k / v appended to the caches, then row i attends to positions
+ * [0, start_pos + i] (the causal mask of src/core/layer.rs:260-269).
+ * d_qkv rows [n_rows][(n_heads + 2*n_kv_heads)*head_dim] (q | k | v);
+ * d_out rows [n_rows][n_heads*head_dim]. */
+int llmrs_attention_prefill(llmrs_ctx *ctx, float *d_qkv, float *d_kcache, float *d_vcache, const float *d_rope_cos,
+                            const float *d_rope_sin, float *d_out, int n_rows, int n_heads, int n_kv_heads,
+                            int head_dim, int max_seq, int start_pos);
+
 /* CpuBackend::quantize_row_q8_0 (src/backend/cpu.rs:663-745) for rows of k
  * values: codes [rows][k] and f32 scales [rows][k/32]; bit-exact */
 int llmrs_quantize_row_q8_0(llmrs_ctx *ctx, const float *d_x, int8_t *d_q, float *d_s, int rows, int k);

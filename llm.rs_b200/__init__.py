@@ -40,7 +40,7 @@ EXPORTS = [
     "llmrs_model_set_weight", "llmrs_kv_fill", "llmrs_kv_fill_synthetic", "llmrs_kv_read",
     "llmrs_decode_step", "llmrs_generate", "llmrs_prefill", "llmrs_model_logits", "llmrs_rope_table",
     "llmrs_model_decode_kernel_count", "llmrs_model_time_decode", "llmrs_model_profile_decode",
-    "llmrs_attention_decode", "llmrs_attention_decode_noalloc", "llmrs_model_trace_decode",
+    "llmrs_attention_decode", "llmrs_attention_decode_noalloc", "llmrs_attention_prefill", "llmrs_model_trace_decode",
     "llmrs_model_tp_region", "llmrs_model_tp_connect", "llmrs_ipc_get_handle", "llmrs_ipc_open_handle",
     "llmrs_ipc_close_handle",
 ]
@@ -126,6 +126,7 @@ def lib():
         "llmrs_model_time_decode": (ci, [vp, ci, ci, ci, fp]),
         "llmrs_model_profile_decode": (ci, [vp, ci, ci, vp, vp, ip]),
         "llmrs_attention_decode": (ci, [vp, vp, vp, vp, vp, vp, vp, ci, ci, ci, ci, ci]),
+        "llmrs_attention_prefill": (ci, [vp, vp, vp, vp, vp, vp, vp, ci, ci, ci, ci, ci, ci]),
         "llmrs_attention_decode_noalloc": (ci, [vp, vp, vp, vp, vp, vp, vp, ci, ci, ci, ci, ci, vp]),
         "llmrs_model_trace_decode": (ci, [vp, ci, ci, vp, vp, ip]),
         "llmrs_model_tp_region": (ci, [vp, pp, ctypes.POINTER(sz)]),
@@ -347,6 +348,15 @@ class CudaBackend:
         max_seq = kcache.shape[1]
         check(lib().llmrs_attention_decode(self.ctx.h, qkv.ptr, kcache.ptr, vcache.ptr, rope_cos.ptr, rope_sin.ptr,
                                            out.ptr, n_heads, n_kv_heads, head_dim, max_seq, pos))
+        return out
+
+    def attention_prefill(self, qkv, kcache, vcache, rope_cos, rope_sin, n_heads, n_kv_heads, head_dim, start_pos):
+        """Causal attention of qkv's rows at start_pos..; RoPEs q in place, appends k/v."""
+        n_rows = qkv.shape[0]
+        out = self._out((n_rows, n_heads * head_dim))
+        max_seq = kcache.shape[1]
+        check(lib().llmrs_attention_prefill(self.ctx.h, qkv.ptr, kcache.ptr, vcache.ptr, rope_cos.ptr, rope_sin.ptr,
+                                            out.ptr, n_rows, n_heads, n_kv_heads, head_dim, max_seq, start_pos))
         return out
 
     # CpuBackend::quantize_row_q8_0 and Tensor::quantize_q4 (bit-exact)

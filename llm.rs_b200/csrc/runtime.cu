@@ -19,6 +19,7 @@
 #include "attention.cuh"
 #include "common.cuh"
 #include "gemv.cuh"
+#include "prefill.cuh"
 #include "step.cuh"
 #include "llmrs_synth.h"
 #include "ops.cuh"
@@ -79,6 +80,7 @@ struct QW {
 
 struct LayerW {
     QW qkv, o, gate_up, down;
+    PrefillWeights p_qkv, p_o, p_gate_up, p_down; // tensor maps of the M>1 (prefill) path
     float *attn_norm = nullptr, *mlp_norm = nullptr;
     float *kc = nullptr, *vc = nullptr;
 };
@@ -172,6 +174,13 @@ struct llmrs_model {
     int *h_stage = nullptr; // 13 slots of 4 ints (token, pos) for H2D; [60..61]: next token, err
     int h_stage_n = 0;
     uint32_t *d_flag = nullptr;
+    // prefill on the tensor cores: row buffers for chunks of up to pf_rows rows
+    int pf_rows = 0;
+    int pf_weights = -1; // -1: not checked, 0: some linear is off the tensor-core path, 1: ready
+    void *pf_buf = nullptr;
+    float *pf_x = nullptr, *pf_qkv = nullptr, *pf_ctx = nullptr, *pf_act = nullptr;
+    int *pf_ids = nullptr;
+    void *pf_acts = nullptr;
 };
 
 // ================================================================== C ABI
@@ -227,6 +236,8 @@ int llmrs_ctx_create(int device, llmrs_ctx **out)
         rc = attention_prepare();
     if (rc == LLMRS_OK)
         rc = step_prepare();
+    if (rc == LLMRS_OK)
+        rc = prefill_prepare();
     if (rc != LLMRS_OK) {
         cudaFree(c->d_err);
         cudaStreamDestroy(c->own);
@@ -337,6 +348,8 @@ int llmrs_sync(llmrs_ctx *ctx)
 }
 
 // ---------------------------------------------------------------- ops
+static int ctx_scratch(llmrs_ctx *ctx, size_t bytes, void **out);
+
 static int gemv_op(llmrs_ctx *ctx, int wf, const float *a, const void *w, const void *scales, int st, float *c,
                    int m, int k, int n)
 {
@@ -344,9 +357,21 @@ static int gemv_op(llmrs_ctx *ctx, int wf, const float *a, const void *w, const 
     LLMRS_CHECK_ARG(m >= 1 && k >= 32 && k % 32 == 0 && n >= 1, "matmul_transposed: m=%d k=%d n=%d (k must be a multiple of 32)", m, k, n);
     LLMRS_CHECK_ARG(st == LLMRS_F16 || st == LLMRS_F32, "scale_dtype %d unknown", st);
     LLMRS_CHECK_ARG(!((uintptr_t)a & 15), "matmul_transposed: activation pointer must be 16-byte aligned");
+    // rows of A are independent (the m>1 path quantises each row, src/backend/cpu.rs:90-110)
+    if (m >= PREFILL_MIN_ROWS) {
+        PrefillWeights pw;
+        LLMRS_TRY(prefill_weights_init(&pw, w, scales, n, k, wf, st));
+        if (pw.ok) { // tensor cores: per-row Q8_0 quantise, then one GEMM over all rows
+            void *scr = nullptr;
+            LLMRS_TRY(ctx_scratch(ctx, prefill_acts_bytes(m, k), &scr));
+            PrefillActs acts;
+            LLMRS_TRY(prefill_acts_init(&acts, scr, m, k, wf));
+            LLMRS_TRY(prefill_quantize(a, k, nullptr, 0.0f, acts, ctx->d_err, ctx->stream));
+            return prefill_gemm(pw, acts, PEPI_STORE, c, n, nullptr, 0, ctx->d_err, ctx->sms, ctx->stream);
+        }
+    }
     GemvPlan plan;
     LLMRS_TRY(gemv_plan(&plan, w, scales, n, k, wf, st, false, ctx->sms));
-    // rows of A are independent (the m>1 path quantises each row, src/backend/cpu.rs:90-110)
     for (int i = 0; i < m; i++) {
         GemvParams p{};
         p.w = reinterpret_cast<const uint8_t *>(w);
@@ -482,6 +507,21 @@ int llmrs_attention_decode(llmrs_ctx *ctx, const float *d_qkv, float *d_kcache, 
     return attention_decode_launch(a, ctx->stream, false);
 }
 
+int llmrs_attention_prefill(llmrs_ctx *ctx, float *d_qkv, float *d_kcache, float *d_vcache, const float *d_rope_cos,
+                            const float *d_rope_sin, float *d_out, int n_rows, int n_heads, int n_kv_heads,
+                            int head_dim, int max_seq, int start_pos)
+{
+    LLMRS_CHECK_ARG(ctx && d_qkv && d_kcache && d_vcache && d_rope_cos && d_rope_sin && d_out, "NULL argument");
+    LLMRS_CHECK_ARG(n_kv_heads > 0 && n_heads > 0 && n_heads % n_kv_heads == 0, "bad head counts %d/%d", n_heads,
+                    n_kv_heads);
+    LLMRS_CHECK_ARG(n_rows > 0 && start_pos >= 0 && max_seq > 0 && start_pos + n_rows <= max_seq,
+                    "rows [%d, %d) outside [0,%d)", start_pos, start_pos + n_rows, max_seq);
+    LLMRS_TRY(prefill_rope_append(d_qkv, d_kcache, d_vcache, d_rope_cos, d_rope_sin, n_rows, start_pos, n_heads,
+                                  n_kv_heads, head_dim, max_seq, ctx->stream));
+    return prefill_attention(d_qkv, d_kcache, d_vcache, d_out, n_rows, start_pos, n_heads, n_kv_heads, head_dim,
+                             max_seq, 1.0f / sqrtf((float)head_dim), ctx->stream);
+}
+
 int llmrs_quantize_row_q8_0(llmrs_ctx *ctx, const float *d_x, int8_t *d_q, float *d_s, int rows, int k)
 {
     LLMRS_CHECK_ARG(ctx && d_x && d_q && d_s && rows >= 0 && k > 0 && k % 32 == 0,
@@ -526,6 +566,8 @@ static void model_free(llmrs_model *m)
         cudaFree(m->tp_region);
     if (m->step_buf)
         cudaFree(m->step_buf);
+    if (m->pf_buf)
+        cudaFree(m->pf_buf);
     if (m->h_stage)
         cudaFreeHost(m->h_stage);
     delete m;
@@ -1276,6 +1318,112 @@ int llmrs_generate(llmrs_model *m, int token, int pos, int n_steps, int *h_token
     return check_state_err(m, (uint32_t)out[1]);
 }
 
+// ------------------------------------------------------------ prefill (M>1)
+constexpr int PF_CHUNK = 512; // rows per tensor-core prefill chunk
+
+// tensor maps of every linear for the M>1 path; false if one is off it
+static int prefill_weights_ready(llmrs_model *m, bool *ready)
+{
+    if (m->pf_weights < 0) {
+        int ok = m->T == 1 ? 1 : 0;
+        for (int l = 0; ok && l < m->cfg.n_layers; l++) {
+            LayerW &L = m->layers[l];
+            const QW *q[4] = {&L.qkv, &L.o, &L.gate_up, &L.down};
+            PrefillWeights *pw[4] = {&L.p_qkv, &L.p_o, &L.p_gate_up, &L.p_down};
+            for (int i = 0; i < 4 && ok; i++) {
+                LLMRS_TRY(prefill_weights_init(pw[i], q[i]->w, q[i]->s, q[i]->n, q[i]->k, m->wf, q[i]->st));
+                ok = pw[i]->ok;
+            }
+        }
+        m->pf_weights = ok;
+    }
+    *ready = m->pf_weights == 1;
+    return LLMRS_OK;
+}
+
+static int prefill_buffers(llmrs_model *m, int rows)
+{
+    if (m->pf_rows >= rows)
+        return LLMRS_OK;
+    if (m->pf_buf)
+        cudaFree(m->pf_buf);
+    m->pf_buf = nullptr;
+    m->pf_rows = 0;
+    const int H = m->H, QD = m->Hq * m->D, NQKV = (m->Hq + 2 * m->Hkv) * m->D, F = m->F;
+    const int kmax = std::max(std::max(H, QD), F);
+    auto up = [](size_t b) { return (b + 1023) & ~size_t(1023); };
+    const size_t bx = up((size_t)rows * H * 4), bq = up((size_t)rows * NQKV * 4), bc = up((size_t)rows * QD * 4),
+                 ba = up((size_t)rows * F * 4), bi = up((size_t)rows * 4), bacts = up(prefill_acts_bytes(rows, kmax));
+    uint8_t *b = nullptr;
+    cudaError_t e = cudaMalloc(&b, bx + bq + bc + ba + bi + bacts);
+    if (e != cudaSuccess)
+        return fail(LLMRS_ENOMEM, "prefill buffers for %d rows: %s", rows, cudaGetErrorString(e));
+    m->pf_buf = b;
+    m->pf_x = reinterpret_cast<float *>(b);
+    m->pf_qkv = reinterpret_cast<float *>(b + bx);
+    m->pf_ctx = reinterpret_cast<float *>(b + bx + bq);
+    m->pf_act = reinterpret_cast<float *>(b + bx + bq + bc);
+    m->pf_ids = reinterpret_cast<int *>(b + bx + bq + bc + ba);
+    m->pf_acts = b + bx + bq + bc + ba + bi;
+    m->pf_rows = rows;
+    return LLMRS_OK;
+}
+
+// Rows start .. start+n-1 through every layer as M = n contractions
+// (src/core/model.rs:17-49 with src/core/layer.rs:160-406 for seq = n): per
+// row RMSNorm + Q8_0, tensor-core QKV, RoPE + KV append, causal attention,
+// o_proj + residual, RMSNorm + gate_up + SiLU*up, down + residual.  Leaves the
+// residual stream of every row in pf_x.
+static int prefill_chunk(llmrs_model *m, const int *h_ids, int n, int start)
+{
+    cudaStream_t s = m->ctx->stream;
+    uint32_t *err = &m->state->err;
+    const int H = m->H, D = m->D, Hq = m->Hq, Hkv = m->Hkv, F = m->F, QD = Hq * D, NQKV = (Hq + 2 * Hkv) * D;
+    const int sms = m->ctx->sms;
+    LLMRS_TRY(prefill_buffers(m, n));
+    LLMRS_CUDA_TRY(cudaMemcpyAsync(m->pf_ids, h_ids, (size_t)n * 4, cudaMemcpyHostToDevice, s));
+    LLMRS_TRY(prefill_embed(m->embed, m->pf_ids, m->pf_x, n, H, m->V, err, s));
+    PrefillActs aH, aQ, aF; // one buffer, three row widths (used one after another)
+    LLMRS_TRY(prefill_acts_init(&aH, m->pf_acts, n, H, m->wf));
+    LLMRS_TRY(prefill_acts_init(&aQ, m->pf_acts, n, QD, m->wf));
+    LLMRS_TRY(prefill_acts_init(&aF, m->pf_acts, n, F, m->wf));
+    const float eps = m->cfg.rms_eps, inv_sqrt_d = 1.0f / sqrtf((float)D);
+    for (int l = 0; l < m->cfg.n_layers; l++) {
+        LayerW &L = m->layers[l];
+        LLMRS_TRY(prefill_quantize(m->pf_x, H, L.attn_norm, eps, aH, err, s));
+        LLMRS_TRY(prefill_gemm(L.p_qkv, aH, PEPI_STORE, m->pf_qkv, NQKV, nullptr, 0, err, sms, s));
+        LLMRS_TRY(prefill_rope_append(m->pf_qkv, L.kc, L.vc, m->rope_cos, m->rope_sin, n, start, Hq, Hkv, D, m->S, s));
+        LLMRS_TRY(prefill_attention(m->pf_qkv, L.kc, L.vc, m->pf_ctx, n, start, Hq, Hkv, D, m->S, inv_sqrt_d, s));
+        LLMRS_TRY(prefill_quantize(m->pf_ctx, QD, nullptr, 0.0f, aQ, err, s));
+        LLMRS_TRY(prefill_gemm(L.p_o, aQ, PEPI_RESIDUAL, m->pf_x, H, m->pf_x, H, err, sms, s));
+        LLMRS_TRY(prefill_quantize(m->pf_x, H, L.mlp_norm, eps, aH, err, s));
+        LLMRS_TRY(prefill_gemm(L.p_gate_up, aH, PEPI_SILU, m->pf_act, F, nullptr, 0, err, sms, s));
+        LLMRS_TRY(prefill_quantize(m->pf_act, F, nullptr, 0.0f, aF, err, s));
+        LLMRS_TRY(prefill_gemm(L.p_down, aF, PEPI_RESIDUAL, m->pf_x, H, m->pf_x, H, err, sms, s));
+    }
+    return LLMRS_OK;
+}
+
+// final RMSNorm + LM head + argmax of one residual row (the batch-1 kernel):
+// the decode state then holds the next token at position pos + 1
+static int prefill_head(llmrs_model *m, const float *x_row, int token, int pos)
+{
+    LLMRS_TRY(set_token_pos(m, token, pos, 0));
+    GemvParams h{};
+    h.err = &m->state->err;
+    h.eps = m->cfg.rms_eps;
+    h.w = m->lm_head.w;
+    h.scales = m->lm_head.s;
+    h.N = m->Vl;
+    h.K = m->H;
+    h.x = x_row;
+    h.norm_w = m->final_norm;
+    h.y = m->logits;
+    h.state = m->state;
+    h.token_log = m->token_log;
+    return gemv_launch(m->lm_head.plan, h, PRO_NORM, EPI_ARGMAX, m->ctx->stream, false);
+}
+
 int llmrs_prefill(llmrs_model *m, const int *h_ids, int n, int start_pos, float *h_logits, int *h_argmax)
 {
     LLMRS_CHECK_ARG(m && h_ids, "NULL argument");
@@ -1286,10 +1434,22 @@ int llmrs_prefill(llmrs_model *m, const int *h_ids, int n, int start_pos, float 
     cudaSetDevice(m->ctx->device);
     LLMRS_TRY(ensure_graph(m));
     cudaStream_t s = m->ctx->stream;
-    // Rows of a prefill chunk are causal and row-independent in every
-    // contraction (src/backend/cpu.rs:90-110, src/core/layer.rs:260-269), so
-    // the chunk is run as n consecutive single-row steps over the same cache.
-    for (int i = 0; i < n; i++) {
+    bool tc = false;
+    if (n >= PREFILL_MIN_ROWS)
+        LLMRS_TRY(prefill_weights_ready(m, &tc));
+    if (tc) {
+        for (int c0 = 0; c0 < n; c0 += PF_CHUNK) {
+            const int rows = std::min(PF_CHUNK, n - c0);
+            LLMRS_TRY(prefill_chunk(m, h_ids + c0, rows, start_pos + c0));
+            if (c0 + rows == n)
+                LLMRS_TRY(prefill_head(m, m->pf_x + (size_t)(rows - 1) * m->H, h_ids[n - 1], start_pos + n - 1));
+        }
+    }
+    // Otherwise (Q4_0 weights, tensor parallel, short prompts): rows of a
+    // prefill chunk are causal and row-independent in every contraction
+    // (src/backend/cpu.rs:90-110, src/core/layer.rs:260-269), so the chunk
+    // runs as n consecutive single-row steps over the same cache.
+    for (int i = 0; !tc && i < n; i++) {
         if (i % 12 == 0 && i > 0)
             LLMRS_CUDA_TRY(cudaStreamSynchronize(s)); // recycle the 12 pinned staging slots
         LLMRS_TRY(set_token_pos(m, h_ids[i], start_pos + i, 1 + (i % 12)));

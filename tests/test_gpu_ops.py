@@ -97,6 +97,39 @@ def test_q8_weight_gemv_bit_exact(llmrs, ctx, be, orc, rng, n, k):
     assert np.array_equal(bits(y), bits(ref))
 
 
+@pytest.mark.parametrize("m,n,k", [(8, 256, 512), (200, 1000, 4096), (512, 512, 4096), (160, 1024, 14336),
+                                   (129, 6144, 4096)])
+@pytest.mark.parametrize("st", [0, 1])
+def test_q8_prefill_gemm_bit_exact(llmrs, ctx, be, orc, rng, m, n, k, st):
+    # M>1 rows on the tcgen05 path (m >= 8, k % 256 == 0): per-row Q8_0
+    # quantise, per-block int8 MMA, in-order f32 block sums -- bit-exact with
+    # the reference's m>1 loop (src/backend/cpu.rs:90-110), ragged m and n
+    qw, sw = orc.synth_q8(7, 2, 14, n, k)
+    a = rng.normal(0, 1, (m, k)).astype(np.float32)
+    a[m // 2, :] = 0.0  # an all-zero row: zero scales, zero outputs
+    W = llmrs.QuantWeight(ctx, qw, sw, n, k, llmrs.WFMT_Q8_0, st)
+    y = be.matmul_transposed(dev(llmrs, ctx, a), W).numpy()
+    ref = orc.matmul_transposed_q8w(a, qw, sw, n)
+    assert y.shape == ref.shape
+    bad = np.argwhere(bits(y) != bits(ref))
+    assert bad.size == 0, (len(bad), bad[:5], np.abs(y - ref).max())
+
+
+@pytest.mark.parametrize("m,n,k", [(8, 256, 512), (300, 1000, 4096), (160, 4096, 14336), (129, 2048, 2048)])
+@pytest.mark.parametrize("st", [0, 1])
+def test_q4_prefill_gemm_bit_exact(llmrs, ctx, be, orc, rng, m, n, k, st):
+    # Q4_0 weights on the tcgen05 path: nibbles unpacked in shared memory to
+    # unsigned codes, the -8 offset folded into the per-block bias
+    qs, sw = orc.synth_q4(5, 1, 11, n, k)
+    a = rng.normal(0, 1, (m, k)).astype(np.float32)
+    a[m // 3, :] = 0.0
+    W = llmrs.QuantWeight(ctx, qs, sw, n, k, llmrs.WFMT_Q4_0, st)
+    y = be.matmul_transposed(dev(llmrs, ctx, a), W).numpy()
+    ref = orc.matmul_transposed_q4(a, qs, sw, n)
+    bad = np.argwhere(bits(y) != bits(ref))
+    assert bad.size == 0, (len(bad), bad[:5], np.abs(y - ref).max())
+
+
 def test_gemv_rejects_bad_k(llmrs, ctx, be, rng):
     a = dev(llmrs, ctx, rng.normal(0, 1, (1, 100)).astype(np.float32))
     W = llmrs.QuantWeight(ctx, np.zeros(50 * 8, np.uint8), np.zeros(8, np.float32), 8, 100)
