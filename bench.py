@@ -3,7 +3,12 @@
 roofline, the end-to-end rate through the C ABI, and the CPU oracle baseline.
 
 python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                [--workload 8b|1b|70b]
+                [--workload 8b|1b|70b] [--no-prefill] [--no-cpu]
+
+On one GPU the line also carries "prefill": config 4 (the 8B shape with Q8_0
+linears), a 512-token prompt through the tensor-core prefill path, timed with
+CUDA events over back-to-back prefills (ids resident), plus its end-to-end
+rate through llmrs_prefill and the CPU oracle's prefill rate.
 
 One "step" = one greedy decode token through every layer + LM head.  Inputs
 (weights 4.2 GB, KV 1.1 GB) are far larger than the 126 MB L2, so no flush is
@@ -41,6 +46,11 @@ WORKLOADS = {
                 kv=2048, name="llama3-70b-shaped Q4_0 decode, KV pre-filled to 2048 (config 5)"),
 }
 SEED = 0x5EED
+
+# config 4: the 8B shape with Q8_0 linears, prefill of a 512-token prompt
+PREFILL = dict(cfg=dict(n_layers=32, hidden=4096, n_heads=32, n_kv_heads=8, head_dim=128, ffn=14336, vocab=128256,
+                        max_seq=576, rms_eps=1e-5, rope_theta=500000.0, weight_format=1, tied_embeddings=0),
+               n=512, name="llama3-8b-shaped Q8_0 prefill of a 512-token prompt (config 4)")
 
 # DRAM bytes per launch of each decode-step GEMV of the 8B shape, from one ncu
 # capture (dram__bytes_read.sum + dram__bytes_write.sum; profiles/
@@ -105,6 +115,19 @@ def gemv_bytes(kind, c):
     if kind == "lm_head_gemv" and c["tied_embeddings"]:
         b += n * k // 16
     return b
+
+
+def prefill_ops(c, n):
+    """Integer MACs x 2 of the linears for n rows (the LM head for the last row
+    only, the row llmrs_prefill returns) and f32 attention FLOPs (QK and PV
+    over the causal triangle)."""
+    lin = sum(2 * nn * k for nn, k in linear_shapes(c)[:-1]) * n + 2 * c["vocab"] * c["hidden"]
+    att = 4 * c["n_layers"] * c["n_heads"] * c["head_dim"] * n * (n + 1) // 2
+    return lin, att
+
+
+def prefill_prompt(c, n):
+    return [(SEED * 31 + 7919 * i) % c["vocab"] for i in range(n)]
 
 
 # ----------------------------------------------------------------- clocks
@@ -187,6 +210,84 @@ def cpu_baseline(wl, n_tokens, threads=None):
         pos += 1
     m.close()
     return 1.0 / statistics.median(times), O.get_threads(), times
+
+
+def cpu_prefill_baseline(threads=None):
+    """The oracle's prefill (the reference's m > 1 path) of a 32-token prompt
+    through 2 layers of the config-4 model, scaled to 32 layers."""
+    from oracle import oracle as O
+    if threads:
+        O.set_threads(threads)
+    c = dict(PREFILL["cfg"], n_layers=2)
+    m = O.Model(c, expand_gqa=True)
+    m.init_synthetic(SEED)
+    ids = prefill_prompt(c, 32)
+    m.forward(ids[:4], 0)  # warm-up
+    t0 = time.perf_counter()
+    m.forward(ids, 0)
+    t = (time.perf_counter() - t0) * PREFILL["cfg"]["n_layers"] / c["n_layers"]
+    m.close()
+    return 32 / t, O.get_threads(), t
+
+
+def int8_peak_tops():
+    """cuBLASLt int8 GEMM throughput (torch._int_mm, 8192^3), the measured
+    int8 tensor peak the prefill is compared with."""
+    import torch
+    n = 8192
+    a = torch.randint(-127, 128, (n, n), dtype=torch.int8, device="cuda")
+    b = torch.randint(-127, 128, (n, n), dtype=torch.int8, device="cuda")
+    for _ in range(3):
+        torch._int_mm(a, b)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(10):
+        torch._int_mm(a, b)
+    e1.record()
+    torch.cuda.synchronize()
+    return 2.0 * n ** 3 / (e0.elapsed_time(e1) / 10 / 1000.0) / 1e12
+
+
+def run_prefill(L, ctx, args):
+    c = PREFILL["cfg"]
+    n = PREFILL["n"]
+    m = L.Model(ctx, dict(c, scale_dtype=L.F16))
+    m.init_synthetic(SEED)
+    ids = prefill_prompt(c, n)
+    m.time_prefill(ids, 0, 3)  # warm-up
+    with ClockSampler(int(os.environ.get("LOCAL_RANK", "0"))) as clk:
+        ms = m.time_prefill(ids, 0, 10)
+    e2e = []
+    for _ in range(3):
+        t0 = time.perf_counter()
+        m.prefill(ids, 0, want_logits=True)
+        e2e.append(time.perf_counter() - t0)
+    m.close()
+    lin, att = prefill_ops(c, n)
+    try:
+        peak = int8_peak_tops()
+    except Exception:
+        peak = None
+    tops = (lin + att) / (ms / 1000.0) / 1e12
+    out = {"metric": "prefill tokens/s", "value": round(n / (ms / 1000.0), 1), "unit": "tokens/s",
+           "ms": round(ms, 3), "workload": PREFILL["name"], "prompt_tokens": n,
+           "dtype": "q8_0 x q8_0 (int8 tensor-core block dots, f32 block sums)",
+           "e2e": {"value": round(n / statistics.median(e2e), 1), "unit": "tokens/s",
+                   "h2d_bytes_per_step": 4 * n, "d2h_bytes_per_step": 4 * c["vocab"] + 8},
+           "ops_per_prefill": {"linear_int_ops": lin, "attention_f32_flops": att},
+           "achieved_tops": round(tops, 1), "clocks": clk.summary()}
+    if peak:
+        out["roofline"] = {"bound": "tensor", "achieved": round(tops, 1), "peak": round(peak, 1), "unit": "TOP/s",
+                           "frac": round(tops / peak, 4),
+                           "peak_source": "measured here: cuBLASLt int8 GEMM 8192^3 (torch._int_mm)",
+                           "note": "the exact per-32-block f32 epilogue (4 f32 ops per block and output) bounds the "
+                                   "GEMM, not the tensor pipe"}
+    if not args.no_cpu:
+        v, cores, t = cpu_prefill_baseline()
+        out["cpu_baseline"] = {"value": round(v, 3), "unit": "tokens/s", "cores": cores, "kind": "port",
+                               "sample": "32-token prompt through 2 of the 32 layers (%.1f s scaled to 32 layers)" % t}
+    return out
 
 
 # ------------------------------------------------------------------ our arm
@@ -303,15 +404,29 @@ def run_ours(args, rank, world):
         "gpu_launches": world * kernels_step * K,
         "clocks": clk.summary(),
     }
+    if world == 1 and args.workload == "8b" and not args.layers and not args.no_prefill:
+        m.close()
+        out["prefill"] = run_prefill(L, ctx, args)
+        m = None
     if rank == 0 and world == 1 and not args.no_cpu:
         n_cpu = 2 if args.workload != "70b" else 1
         v, cores, times = cpu_baseline(wl, n_cpu)
         out["cpu_baseline"] = {"value": round(v, 3), "unit": "tokens/s", "cores": cores, "kind": "port",
                                "sample": "%d decode tokens of the same model at KV %d (median of %s s)" %
                                          (n_cpu, kv0 + 1, [round(t, 2) for t in times])}
-    m.close()
+    if m is not None:
+        m.close()
     ctx.close()
     return out
+
+
+def prefill_reference(args):
+    if args.workload != "8b" or args.no_prefill:
+        return None
+    v, cores, t = cpu_prefill_baseline()
+    return {"metric": "prefill tokens/s", "value": round(v, 3), "unit": "tokens/s", "workload": PREFILL["name"],
+            "cpu_baseline": {"value": round(v, 3), "unit": "tokens/s", "cores": cores, "kind": "port",
+                             "sample": "32-token prompt through 2 of the 32 layers (%.1f s scaled to 32 layers)" % t}}
 
 
 def run_reference(args, rank, world):
@@ -334,6 +449,7 @@ def run_reference(args, rank, world):
                          "sample": "%d decode tokens at KV %d; reference CPU path restated in C (oracle/), "
                                    "Rust reference not buildable here" % (n, wl["kv"] + 1)},
         "e2e": {"value": round(v, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "prefill": prefill_reference(args),
     }
 
 
@@ -345,6 +461,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="8b")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-prefill", action="store_true", help="skip the config-4 prefill leg")
     ap.add_argument("--layers", type=int, default=0,
                     help="override the layer count (small cases for ncu captures; not a bench line)")
     args = ap.parse_args()

@@ -226,8 +226,15 @@ int llmrs_decode_step(llmrs_model *model, int token, int pos, float *h_logits, i
 int llmrs_generate(llmrs_model *model, int token, int pos, int n_steps, int *h_tokens_out);
 /* prefill n prompt tokens at positions [start_pos, start_pos+n) (src/main.rs:134-138
  * chunk, the m>1 path of src/backend/cpu.rs:90-110); writes the last row's
- * logits / argmax like llmrs_decode_step */
+ * logits / argmax like llmrs_decode_step.  On one GPU, n >= 8 rows with every
+ * linear's K a multiple of 256 run as M = n contractions on the tensor cores
+ * (chunks of 512 rows; the LM head on the last row only, the row the caller
+ * reads at src/main.rs:185-190); otherwise as n single-row steps. */
 int llmrs_prefill(llmrs_model *model, const int *h_ids, int n, int start_pos, float *h_logits, int *h_argmax);
+/* device time (CUDA events) of one tensor-core prefill of h_ids, averaged over
+ * iters back-to-back prefills with the ids already on the device;
+ * LLMRS_ENOTSUP when the prompt/model takes the single-row path */
+int llmrs_model_time_prefill(llmrs_model *model, const int *h_ids, int n, int start_pos, int iters, float *ms_out);
 /* read the last decode/prefill logits (device resident) into h_logits[vocab] */
 int llmrs_model_logits(llmrs_model *model, float *h_logits);
 /* host-only helper: the RoPE cos/sin table the decode step uses, [n_pos][head_dim/2]

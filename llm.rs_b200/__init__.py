@@ -39,7 +39,8 @@ EXPORTS = [
     "llmrs_quantize_q4", "llmrs_model_create", "llmrs_model_destroy", "llmrs_model_init_synthetic",
     "llmrs_model_set_weight", "llmrs_kv_fill", "llmrs_kv_fill_synthetic", "llmrs_kv_read",
     "llmrs_decode_step", "llmrs_generate", "llmrs_prefill", "llmrs_model_logits", "llmrs_rope_table",
-    "llmrs_model_decode_kernel_count", "llmrs_model_time_decode", "llmrs_model_profile_decode",
+    "llmrs_model_decode_kernel_count", "llmrs_model_time_decode", "llmrs_model_time_prefill",
+    "llmrs_model_profile_decode",
     "llmrs_attention_decode", "llmrs_attention_decode_noalloc", "llmrs_attention_prefill", "llmrs_model_trace_decode",
     "llmrs_model_tp_region", "llmrs_model_tp_connect", "llmrs_ipc_get_handle", "llmrs_ipc_open_handle",
     "llmrs_ipc_close_handle",
@@ -124,6 +125,7 @@ def lib():
         "llmrs_rope_table": (ci, [ci, ci, cf, vp, vp]),
         "llmrs_model_decode_kernel_count": (ci, [vp, ip]),
         "llmrs_model_time_decode": (ci, [vp, ci, ci, ci, fp]),
+        "llmrs_model_time_prefill": (ci, [vp, vp, ci, ci, ci, fp]),
         "llmrs_model_profile_decode": (ci, [vp, ci, ci, vp, vp, ip]),
         "llmrs_attention_decode": (ci, [vp, vp, vp, vp, vp, vp, vp, ci, ci, ci, ci, ci]),
         "llmrs_attention_prefill": (ci, [vp, vp, vp, vp, vp, vp, vp, ci, ci, ci, ci, ci, ci]),
@@ -519,6 +521,14 @@ class Model:
     def time_decode(self, token, pos, iters):
         ms = ctypes.c_float(0)
         check(lib().llmrs_model_time_decode(self.h, int(token), int(pos), int(iters), ctypes.byref(ms)))
+        return ms.value
+
+    def time_prefill(self, ids, start_pos, iters):
+        """Device ms of one tensor-core prefill of `ids` (mean of `iters`)."""
+        ids = np.ascontiguousarray(ids, np.int32)
+        ms = ctypes.c_float(0)
+        check(lib().llmrs_model_time_prefill(self.h, _ptr(ids), ids.size, int(start_pos), int(iters),
+                                             ctypes.byref(ms)))
         return ms.value
 
 

@@ -1353,7 +1353,7 @@ static int prefill_buffers(llmrs_model *m, int rows)
     const int kmax = std::max(std::max(H, QD), F);
     auto up = [](size_t b) { return (b + 1023) & ~size_t(1023); };
     const size_t bx = up((size_t)rows * H * 4), bq = up((size_t)rows * NQKV * 4), bc = up((size_t)rows * QD * 4),
-                 ba = up((size_t)rows * F * 4), bi = up((size_t)rows * 4), bacts = up(prefill_acts_bytes(rows, kmax));
+                 ba = up((size_t)rows * F * 4), bi = up((size_t)m->S * 4), bacts = up(prefill_acts_bytes(rows, kmax));
     uint8_t *b = nullptr;
     cudaError_t e = cudaMalloc(&b, bx + bq + bc + ba + bi + bacts);
     if (e != cudaSuccess)
@@ -1374,15 +1374,13 @@ static int prefill_buffers(llmrs_model *m, int rows)
 // row RMSNorm + Q8_0, tensor-core QKV, RoPE + KV append, causal attention,
 // o_proj + residual, RMSNorm + gate_up + SiLU*up, down + residual.  Leaves the
 // residual stream of every row in pf_x.
-static int prefill_chunk(llmrs_model *m, const int *h_ids, int n, int start)
+static int prefill_chunk(llmrs_model *m, const int *d_ids, int n, int start)
 {
     cudaStream_t s = m->ctx->stream;
     uint32_t *err = &m->state->err;
     const int H = m->H, D = m->D, Hq = m->Hq, Hkv = m->Hkv, F = m->F, QD = Hq * D, NQKV = (Hq + 2 * Hkv) * D;
     const int sms = m->ctx->sms;
-    LLMRS_TRY(prefill_buffers(m, n));
-    LLMRS_CUDA_TRY(cudaMemcpyAsync(m->pf_ids, h_ids, (size_t)n * 4, cudaMemcpyHostToDevice, s));
-    LLMRS_TRY(prefill_embed(m->embed, m->pf_ids, m->pf_x, n, H, m->V, err, s));
+    LLMRS_TRY(prefill_embed(m->embed, d_ids, m->pf_x, n, H, m->V, err, s));
     PrefillActs aH, aQ, aF; // one buffer, three row widths (used one after another)
     LLMRS_TRY(prefill_acts_init(&aH, m->pf_acts, n, H, m->wf));
     LLMRS_TRY(prefill_acts_init(&aQ, m->pf_acts, n, QD, m->wf));
@@ -1424,6 +1422,59 @@ static int prefill_head(llmrs_model *m, const float *x_row, int token, int pos)
     return gemv_launch(m->lm_head.plan, h, PRO_NORM, EPI_ARGMAX, m->ctx->stream, false);
 }
 
+// the ids already in pf_ids: every chunk, then the LM head on the last row
+static int prefill_rows(llmrs_model *m, int n, int start_pos, int last_id)
+{
+    for (int c0 = 0; c0 < n; c0 += PF_CHUNK) {
+        const int rows = std::min(PF_CHUNK, n - c0);
+        LLMRS_TRY(prefill_chunk(m, m->pf_ids + c0, rows, start_pos + c0));
+        if (c0 + rows == n)
+            LLMRS_TRY(prefill_head(m, m->pf_x + (size_t)(rows - 1) * m->H, last_id, start_pos + n - 1));
+    }
+    return LLMRS_OK;
+}
+
+int llmrs_model_time_prefill(llmrs_model *m, const int *h_ids, int n, int start_pos, int iters, float *ms_out)
+{
+    LLMRS_CHECK_ARG(m && h_ids && ms_out && iters > 0, "bad arguments");
+    LLMRS_CHECK_ARG(n >= 1 && start_pos >= 0 && start_pos + n <= m->S, "prefill of %d tokens at %d exceeds max_seq %d",
+                    n, start_pos, m->S);
+    for (int i = 0; i < n; i++)
+        LLMRS_CHECK_ARG(h_ids[i] >= 0 && h_ids[i] < m->V, "token id %d at %d out of range", h_ids[i], i);
+    cudaSetDevice(m->ctx->device);
+    LLMRS_TRY(ensure_graph(m));
+    bool tc = false;
+    if (n >= PREFILL_MIN_ROWS)
+        LLMRS_TRY(prefill_weights_ready(m, &tc));
+    if (!tc)
+        return fail(LLMRS_ENOTSUP, "this model/prompt does not take the tensor-core prefill path");
+    cudaStream_t s = m->ctx->stream;
+    LLMRS_TRY(prefill_buffers(m, std::min(n, PF_CHUNK)));
+    LLMRS_CUDA_TRY(cudaMemcpyAsync(m->pf_ids, h_ids, (size_t)n * 4, cudaMemcpyHostToDevice, s));
+    cudaEvent_t e0, e1;
+    LLMRS_CUDA_TRY(cudaEventCreate(&e0));
+    LLMRS_CUDA_TRY(cudaEventCreate(&e1));
+    int rc = LLMRS_OK;
+    cudaEventRecord(e0, s);
+    for (int i = 0; i < iters && rc == LLMRS_OK; i++)
+        rc = prefill_rows(m, n, start_pos, h_ids[n - 1]);
+    cudaEventRecord(e1, s);
+    cudaError_t e = cudaEventSynchronize(e1);
+    float ms = 0.0f;
+    if (e == cudaSuccess)
+        e = cudaEventElapsedTime(&ms, e0, e1);
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    if (rc != LLMRS_OK)
+        return rc;
+    if (e != cudaSuccess)
+        return fail(LLMRS_ECUDA, "prefill timing: %s", cudaGetErrorString(e));
+    *ms_out = ms / iters;
+    uint32_t err = 0;
+    LLMRS_CUDA_TRY(cudaMemcpy(&err, &m->state->err, 4, cudaMemcpyDeviceToHost));
+    return check_state_err(m, err);
+}
+
 int llmrs_prefill(llmrs_model *m, const int *h_ids, int n, int start_pos, float *h_logits, int *h_argmax)
 {
     LLMRS_CHECK_ARG(m && h_ids, "NULL argument");
@@ -1438,12 +1489,9 @@ int llmrs_prefill(llmrs_model *m, const int *h_ids, int n, int start_pos, float 
     if (n >= PREFILL_MIN_ROWS)
         LLMRS_TRY(prefill_weights_ready(m, &tc));
     if (tc) {
-        for (int c0 = 0; c0 < n; c0 += PF_CHUNK) {
-            const int rows = std::min(PF_CHUNK, n - c0);
-            LLMRS_TRY(prefill_chunk(m, h_ids + c0, rows, start_pos + c0));
-            if (c0 + rows == n)
-                LLMRS_TRY(prefill_head(m, m->pf_x + (size_t)(rows - 1) * m->H, h_ids[n - 1], start_pos + n - 1));
-        }
+        LLMRS_TRY(prefill_buffers(m, std::min(n, PF_CHUNK)));
+        LLMRS_CUDA_TRY(cudaMemcpyAsync(m->pf_ids, h_ids, (size_t)n * 4, cudaMemcpyHostToDevice, s));
+        LLMRS_TRY(prefill_rows(m, n, start_pos, h_ids[n - 1]));
     }
     // Otherwise (Q4_0 weights, tensor parallel, short prompts): rows of a
     // prefill chunk are causal and row-independent in every contraction
