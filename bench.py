@@ -250,14 +250,16 @@ def int8_peak_tops():
 
 
 def run_prefill(L, ctx, args):
-    c = PREFILL["cfg"]
+    c = dict(PREFILL["cfg"])
+    if args.layers:
+        c["n_layers"] = args.layers
     n = PREFILL["n"]
     m = L.Model(ctx, dict(c, scale_dtype=L.F16))
     m.init_synthetic(SEED)
     ids = prefill_prompt(c, n)
-    m.time_prefill(ids, 0, 3)  # warm-up
+    m.time_prefill(ids, 0, args.warmup)  # warm-up
     with ClockSampler(int(os.environ.get("LOCAL_RANK", "0"))) as clk:
-        ms = m.time_prefill(ids, 0, 10)
+        ms = m.time_prefill(ids, 0, max(1, min(args.steps, 10)))
     e2e = []
     for _ in range(3):
         t0 = time.perf_counter()
@@ -462,6 +464,8 @@ def main():
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="8b")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-prefill", action="store_true", help="skip the config-4 prefill leg")
+    ap.add_argument("--prefill-only", action="store_true",
+                    help="run only the config-4 prefill leg (with --layers: a small case for ncu; not a bench line)")
     ap.add_argument("--layers", type=int, default=0,
                     help="override the layer count (small cases for ncu captures; not a bench line)")
     args = ap.parse_args()
@@ -473,7 +477,12 @@ def main():
 
         import torch.distributed as dist
         dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
-    if args.impl == "reference":
+    if args.prefill_only:
+        L = load_pkg()
+        ctx = L.Context(int(os.environ.get("LOCAL_RANK", "0")))
+        out = run_prefill(L, ctx, args)
+        ctx.close()
+    elif args.impl == "reference":
         out = run_reference(args, rank, world)
     else:
         out = run_ours(args, rank, world)

@@ -442,9 +442,10 @@ __global__ void __launch_bounds__(PG_THREADS, 1)
                 for (int j = 0; j < 8; j++) {
                     const float *saj = sas + j * PG_TILE;
                     const int *acj = acs + j * PG_TILE;
+                    const float swj = sw[j];
                     tmem_wait_ld(ra);
                     tmem_ld16(tl + buf_of(g) + 16, rb);
-                    block_sum16<WF>(acc, ra, sw[j], saj, acj);
+                    block_sum16<WF>(acc, ra, swj, saj, acj);
                     tmem_wait_ld(rb);
                     tc_fence_before();
                     __syncwarp();
@@ -458,7 +459,7 @@ __global__ void __launch_bounds__(PG_THREADS, 1)
                         if (ok)
                             tmem_ld16(tl + buf_of(g), ra);
                     }
-                    block_sum16<WF>(acc + 16, rb, sw[j], saj + 16, acj + 16);
+                    block_sum16<WF>(acc + 16, rb, swj, saj + 16, acj + 16);
                     if (!ok)
                         break;
                 }
