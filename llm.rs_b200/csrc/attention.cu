@@ -21,6 +21,7 @@
 // warps of a CTA merge through shared memory, split partials (m, l, acc) go
 // to global memory, and the last CTA of each KV head merges them in split
 // order.
+#include <stdlib.h>
 #include <mutex>
 
 #include "attention.cuh"
@@ -131,6 +132,11 @@ __global__ void __launch_bounds__(AttnWarps<D>::value * 32, 1) attn_decode_kerne
             trace_start(p.trace, p.trace_slot);
         }
         fence_mbar_init();
+        // K/V rows of the cached positions [0, pos) were written by earlier
+        // steps, not by the kernel this one may overlap: the first chunks
+        // stream before the dependency wait
+        for (int j = 0; j < p.early && j < 2 && j < mine; j++)
+            issue(j, policy_evict_first());
     }
 
     griddep_wait();
@@ -165,7 +171,7 @@ __global__ void __launch_bounds__(AttnWarps<D>::value * 32, 1) attn_decode_kerne
     __syncthreads(); // small loads issued; barriers initialised
     if (lane == 0) {
         const uint64_t pol = policy_evict_first();
-        for (int j = 0; j < 2 && j < mine; j++)
+        for (int j = p.early < 0 ? 0 : p.early; j < 2 && j < mine; j++)
             issue(j, pol);
     }
     __syncwarp();
@@ -402,8 +408,21 @@ size_t attention_partials_floats(int n_heads, int head_dim, int n_splits)
     return (size_t)n_heads * n_splits * (head_dim + 2);
 }
 
-int attention_decode_launch(const AttnParams &p, cudaStream_t stream, bool pdl)
+// chunks per warp issued before the dependency wait (LLMRS_ATTN_EARLY, 0..2)
+static int attn_early(void)
 {
+    static const int n = [] {
+        const char *e = getenv("LLMRS_ATTN_EARLY");
+        const int v = e ? atoi(e) : 1;
+        return v < 0 ? 0 : (v > 2 ? 2 : v);
+    }();
+    return n;
+}
+
+int attention_decode_launch(const AttnParams &p0, cudaStream_t stream, bool pdl)
+{
+    AttnParams p = p0;
+    p.early = attn_early();
     LLMRS_CHECK_ARG(p.n_kv > 0 && p.n_heads % p.n_kv == 0, "attention: n_heads %d not a multiple of n_kv %d",
                     p.n_heads, p.n_kv);
     const int nrep = p.n_heads / p.n_kv;

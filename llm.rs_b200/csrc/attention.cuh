@@ -23,6 +23,7 @@ struct AttnParams {
     unsigned long long *trace; // optional timeline (see GemvParams)
     int trace_slot;
     int n_heads, n_kv, head_dim, max_seq, n_splits;
+    int early;               // K/V chunks per warp requested before the dependency wait (set at launch)
     float inv_sqrt_d;        // 1 / sqrt(D), as src/core/layer.rs:258 computes it
 };
 
