@@ -98,14 +98,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         }
         return;
     }
-    LLMRS_TRACE_BEGIN(1);
-    griddep_wait();
-    LLMRS_TRACE_END(1);
     const int ctid = threadIdx.x;
-    if (ctid == 0)
-        trace_go(p.trace, p.trace_slot);
     uint32_t cpar = 0, lpar = 0;
-    gemv_consume<WF, ST, PRO, EPI>(p, w, sm, cpar, lpar, ctid);
+    gemv_consume<WF, ST, PRO, EPI>(p, w, sm, cpar, lpar, ctid, true); // waits for the previous kernel itself
     LLMRS_TRACE_FLUSH(0);
     if (ctid == 0)
         trace_end(p.trace, p.trace_slot);

@@ -237,12 +237,20 @@ __device__ __forceinline__ void quantize_block8(const float (&v)[4], int j, bool
 // fused): 4 rounds with a norm (x and its weights), 8 without; later rounds
 // (larger K) load as they go.
 
+// dep_wait: this thread has not yet waited for the previous kernel; the loads
+// that do not depend on it (RMSNorm weights) are issued first, then the wait.
 template <int WF, int PRO>
 __device__ __forceinline__ void load_activation(const GemvParams &p, uint32_t *act, float *act_s, int *act_c, float *red, int tid,
-                                int nthr, int bar, uint64_t *issued)
+                                int nthr, int bar, uint64_t *issued, bool dep_wait = false)
 {
     const int K = p.K, nb = K >> 5;
     const bool has = tid < nb;
+    constexpr bool EARLY_W = PRO == PRO_NORM || PRO == PRO_EMBED_NORM; // norm weights loaded before the wait
+    if (!EARLY_W && dep_wait) {
+        griddep_wait();
+        if (tid == 0)
+            trace_go(p.trace, p.trace_slot);
+    }
     if (PRO == PRO_Q8) {
         uint4 c0 = make_uint4(0, 0, 0, 0), c1 = c0;
         float xs = 0.0f;
@@ -328,14 +336,24 @@ __device__ __forceinline__ void load_activation(const GemvParams &p, uint32_t *a
     };
     const bool store_x = (PRO == PRO_EMBED_NORM || AR) && blockIdx.x == 0; // the residual stream's new value
     float xv[ACT_ROUNDS][4], wv[NORM ? ACT_ROUNDS : 1][4];
+    if (NORM) { // the RMSNorm weights do not depend on the previous kernel
+#pragma unroll
+        for (int r = 0; r < ACT_ROUNDS; r++) {
+            const int b = (r * nwarps + warp) * 4 + sub;
+            if (r < rounds && b < nb)
+                load4w(b, wv[NORM ? r : 0]);
+        }
+        if (EARLY_W && dep_wait) {
+            griddep_wait();
+            if (tid == 0)
+                trace_go(p.trace, p.trace_slot);
+        }
+    }
 #pragma unroll
     for (int r = 0; r < ACT_ROUNDS; r++) {
         const int b = (r * nwarps + warp) * 4 + sub;
-        if (r < rounds && b < nb) {
+        if (r < rounds && b < nb)
             load4(b, xv[r]);
-            if (NORM)
-                load4w(b, wv[NORM ? r : 0]);
-        }
     }
     if (!AR)
         signal_issued(issued, tid);
@@ -714,18 +732,19 @@ __device__ __forceinline__ bool gemv_produce(const CUtensorMap *tw, const CUtens
 // Consumers (the NW consumer warps, ctid = 0 .. NW*32-1): prologue, steps,
 // epilogue of one GEMV.  cpar / lpar: per stage, parity of the full-barrier
 // phase to wait for next; per warp, parity of its link arrivals so far (kept
-// across ops; advanced to the op's end on return).  The caller has already
-// waited for the op's input.
+// across ops; advanced to the op's end on return).  dep_wait: the prologue
+// waits for the previous kernel itself (after the loads that do not depend on
+// it); otherwise the caller has already waited for the op's input.
 template <int WF, int ST, int PRO, int EPI>
 __device__ __forceinline__ void gemv_consume(const GemvParams &p, const GemvWork &w, const GemvSmem &sm, uint32_t &cpar,
-                             uint32_t &lpar, int ctid)
+                             uint32_t &lpar, int ctid, bool dep_wait = false)
 {
     constexpr int W_ROW = CB * wbytes_per_block(WF);
     constexpr int S_ROW = CB * sbytes(ST);
     const int warp = ctid >> 5, lane = ctid & 31;
     const int SPG = sm.S / NG;
     LLMRS_TRACE_BEGIN(2);
-    load_activation<WF, PRO>(p, sm.act, sm.act_s, sm.act_c, sm.red, ctid, PRO_THREADS, 1, sm.issued);
+    load_activation<WF, PRO>(p, sm.act, sm.act_s, sm.act_c, sm.red, ctid, PRO_THREADS, 1, sm.issued, dep_wait);
     named_bar_sync(1, PRO_THREADS);
     if (ctid == 0) {
         trace_ready(p.trace, p.trace_slot);

@@ -35,6 +35,9 @@ namespace llmrs {
 
 namespace {
 
+// the row quantiser runs the batch-1 GEMV's prologue with its thread count, so
+// both paths sum the RMSNorm squares in the same order
+constexpr int PG_QUANT_THREADS = PRO_THREADS;
 constexpr int PG_TBUF = 4;                           // TMEM accumulator buffers (128 columns each)
 constexpr int PG_EPI_WARPS = 16;
 constexpr int PG_THREADS = (2 + PG_EPI_WARPS) * 32;  // producer warp, MMA warp, epilogue warps
@@ -579,91 +582,228 @@ __global__ void prefill_rope_append_kernel(float *qkv, float *kc, float *vc, con
 }
 
 // ------------------------------------------------------------- attention
-constexpr int PA_ROWS = 16;   // query rows per CTA (one warp each)
-constexpr int PA_CH = 32;     // cached positions per shared-memory chunk
+// CTA = (RB query rows, KV head g): the RB * NREP = 64 query vectors of the
+// NREP heads of g share every K/V chunk of 32 positions, staged in shared
+// memory with cp.async (double-buffered).  Per chunk:
+//   scores: thread = 2 query vectors x 4 positions; each score sums q[d]*k[d]
+//     for d = 0..D-1 in order, unfused, then * 1/sqrt(D) -- bit-exact with
+//     the reference's f32 dot (src/backend/cpu.rs:458-551, non-aarch64) --
+//     and positions past the row's own are masked (src/core/layer.rs:260-269);
+//   online softmax per query vector (8 lanes share one);
+//   P.V: thread = 4 query vectors x D/16 dims, f32 FMA.
+constexpr int PA_KC = 32;       // positions per chunk
+constexpr int PA_QV = 64;       // query vectors per CTA
+constexpr int PA_THREADS = 256;
 
-template <int D, int NREP>
+template <int D>
 struct PaLayout {
-    static constexpr int QS = D + 4; // q row stride (floats): heads on distinct banks
-    static constexpr int K_OFF = 0;
-    static constexpr int V_OFF = K_OFF + PA_CH * D * 4;
-    static constexpr int Q_OFF = V_OFF + PA_CH * D * 4;
-    static constexpr int P_OFF = Q_OFF + PA_ROWS * NREP * QS * 4;
-    static constexpr int BYTES = P_OFF + PA_ROWS * 64 * 4;
+    static constexpr int QS = D + 4;                                     // padded rows: conflict-free 16-byte loads
+    static constexpr int Q_OFF = 0;                                      // [PA_QV][QS]
+    static constexpr int K_OFF = Q_OFF + PA_QV * QS * 4;                 // [2][PA_KC][QS]
+    static constexpr int V_OFF = K_OFF + 2 * PA_KC * QS * 4;             // [2][PA_KC][D]
+    static constexpr int PS = PA_QV + 4;                                 // padded probability rows
+    static constexpr int P_OFF = V_OFF + 2 * PA_KC * D * 4;              // [PA_KC][PS] probabilities
+    static constexpr int C_OFF = P_OFF + PA_KC * PS * 4;                 // [PA_QV] rescale of the running sums
+    static constexpr int BYTES = C_OFF + PA_QV * 4;
 };
 
-// CTA (row block, KV head g): warp w takes query row m0 + w (position
-// start + m0 + w) and the NREP query heads of g; K/V chunks are staged once
-// for the CTA and each warp runs the batch-1 chunk step (bit-exact scores,
-// online softmax) over the positions it may see.
-template <int D, int NREP>
-__global__ void __launch_bounds__(PA_ROWS * 32) prefill_attention_kernel(const float *qkv, const float *kc,
-                                                                         const float *vc, float *ctx, int M,
-                                                                         int start, int Hq, int Hkv, int S,
-                                                                         float inv_sqrt_d)
+__device__ __forceinline__ void cp_async16(void *dst, const void *src, bool valid)
 {
-    using L = PaLayout<D, NREP>;
-    constexpr int DL = D / 32;
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_addr(dst)), "l"(src),
+                 "r"(valid ? 16 : 0)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_0() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
+template <int D, int NREP>
+__global__ void __launch_bounds__(PA_THREADS, 2) prefill_attention_kernel(const float *qkv, const float *kc,
+                                                                          const float *vc, float *ctx, int M,
+                                                                          int start, int Hq, int Hkv, int S,
+                                                                          float inv_sqrt_d)
+{
+    using Lay = PaLayout<D>;
+    constexpr int RB = PA_QV / NREP; // query rows per CTA
+    constexpr int QS = Lay::QS;
+    constexpr int DPT = D / 16;      // P.V dims per thread
     extern __shared__ __align__(16) uint8_t pasm[];
-    float *ks = reinterpret_cast<float *>(pasm + L::K_OFF);
-    float *vs = reinterpret_cast<float *>(pasm + L::V_OFF);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int g = blockIdx.y, m0 = blockIdx.x * PA_ROWS;
-    const int m = m0 + warp;
-    const bool live = m < M;
-    const int pos = start + m;
-    float *q_s = reinterpret_cast<float *>(pasm + L::Q_OFF) + warp * NREP * L::QS;
-    float *probs = reinterpret_cast<float *>(pasm + L::P_OFF) + warp * 64;
+    float *q_s = reinterpret_cast<float *>(pasm + Lay::Q_OFF);
+    float *k_s = reinterpret_cast<float *>(pasm + Lay::K_OFF);
+    float *v_s = reinterpret_cast<float *>(pasm + Lay::V_OFF);
+    float *p_s = reinterpret_cast<float *>(pasm + Lay::P_OFF);
+    float *c_s = reinterpret_cast<float *>(pasm + Lay::C_OFF);
+    const int tid = threadIdx.x, lane = tid & 31;
+    const int g = blockIdx.y, m0 = blockIdx.x * RB;
     const int ld = (Hq + 2 * Hkv) * D;
-    if (live)
-        for (int e = lane; e < NREP * D; e += 32) {
-            const int h = e / D, d = e % D;
-            q_s[h * L::QS + d] = qkv[(size_t)m * ld + (size_t)(g * NREP + h) * D + d];
-        }
-    const int last = start + min(m0 + PA_ROWS, M) - 1; // highest position any row of the CTA sees
+    const int rows = min(RB, M - m0);
+    const int last = start + m0 + rows - 1; // highest position any row of the CTA sees
+    const int nch = last / PA_KC + 1;
     const float *kg = kc + (size_t)g * S * D;
     const float *vg = vc + (size_t)g * S * D;
-    float m_run = -INFINITY, l_run = 0.0f;
-    float acc[NREP][DL];
-#pragma unroll
-    for (int h = 0; h < NREP; h++)
-#pragma unroll
-        for (int k = 0; k < DL; k++)
-            acc[h][k] = 0.0f;
-    for (int t0 = 0; t0 <= last; t0 += PA_CH) {
-        __syncthreads(); // previous chunk consumed (and q_s written)
-        for (int e = threadIdx.x; e < PA_CH * D / 4; e += PA_ROWS * 32) {
-            const int r = e / (D / 4), d = (e % (D / 4)) * 4;
+
+    // chunk loader: K rows into padded rows, V rows plain; positions past
+    // `last` are zero-filled (and masked)
+    auto load_chunk = [&](int c, int buf) {
+        const int t0 = c * PA_KC;
+        for (int e = tid; e < PA_KC * D / 4; e += PA_THREADS) {
+            const int r = e / (D / 4), d4 = e % (D / 4);
             const int t = t0 + r;
-            float4 kv = make_float4(0.0f, 0.0f, 0.0f, 0.0f), vv = kv;
-            if (t <= last) {
-                kv = *reinterpret_cast<const float4 *>(kg + (size_t)t * D + d);
-                vv = *reinterpret_cast<const float4 *>(vg + (size_t)t * D + d);
-            }
-            *reinterpret_cast<float4 *>(ks + kswz<PA_CH>(r, d)) = kv;
-            *reinterpret_cast<float4 *>(vs + r * D + d) = vv;
+            const bool ok = t <= last;
+            const size_t off = (size_t)(ok ? t : 0) * D + d4 * 4;
+            cp_async16(k_s + (size_t)(buf * PA_KC + r) * QS + d4 * 4, kg + off, ok);
+            cp_async16(v_s + (size_t)(buf * PA_KC + r) * D + d4 * 4, vg + off, ok);
         }
-        __syncthreads();
-        if (live && t0 <= pos) {
-#pragma unroll 1
-            for (int r0 = 0; r0 < PA_CH; r0 += 8) {
-                const int nvalid = min(8, pos + 1 - (t0 + r0));
-                if (nvalid <= 0)
-                    break;
-                attn_chunk<D, NREP, PA_CH>(ks, r0, vs + r0 * D, nvalid, q_s, L::QS, probs, inv_sqrt_d, m_run,
-                                           l_run, acc, lane);
-            }
-        }
+        cp_async_commit();
+    };
+    load_chunk(0, 0);
+    // query vectors qv = r * NREP + h (row m0 + r, head g*NREP + h)
+    for (int e = tid; e < PA_QV * D / 4; e += PA_THREADS) {
+        const int qv = e / (D / 4), d4 = e % (D / 4);
+        const int r = qv / NREP, h = qv % NREP;
+        float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (r < rows)
+            v = *reinterpret_cast<const float4 *>(qkv + (size_t)(m0 + r) * ld + (size_t)(g * NREP + h) * D + d4 * 4);
+        *reinterpret_cast<float4 *>(q_s + qv * QS + d4 * 4) = v;
     }
-    if (!live)
-        return;
+
+    // score-phase roles: query vectors sq, sq+1; positions kq, kq+8, kq+16,
+    // kq+24 of the chunk (8 lanes read 8 consecutive K rows: distinct banks)
+    constexpr int PS = Lay::PS;
+    const int sq = (tid >> 3) * 2, kq = tid & 7;
+    int pos_s[2];
 #pragma unroll
-    for (int h = 0; h < NREP; h++) {
-        const float l = __shfl_sync(0xffffffffu, l_run, h);
-        float *dst = ctx + (size_t)m * Hq * D + (size_t)(g * NREP + h) * D + lane * DL;
+    for (int i = 0; i < 2; i++)
+        pos_s[i] = start + m0 + (sq + i) / NREP;
+    float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.0f, 0.0f};
+    // P.V roles: query vectors oq .. oq+3, dims od .. od+DPT-1
+    const int oq = (tid >> 4) * 4, od = (tid & 15) * DPT;
+    float o[4][DPT];
 #pragma unroll
-        for (int k = 0; k < DL; k++)
-            dst[k] = acc[h][k] / l;
+    for (int i = 0; i < 4; i++)
+#pragma unroll
+        for (int j = 0; j < DPT; j++)
+            o[i][j] = 0.0f;
+
+    for (int c = 0; c < nch; c++) {
+        const int buf = c & 1;
+        if (c + 1 < nch) {
+            load_chunk(c + 1, buf ^ 1);
+            cp_async_wait_1();
+        } else {
+            cp_async_wait_0();
+        }
+        __syncthreads(); // chunk c (and q_s) visible
+        const float *kb = k_s + (size_t)buf * PA_KC * QS;
+        const float *vb = v_s + (size_t)buf * PA_KC * D;
+        // ---- scores, d in order, unfused
+        float sc[2][4];
+#pragma unroll
+        for (int i = 0; i < 2; i++)
+#pragma unroll
+            for (int j = 0; j < 4; j++)
+                sc[i][j] = 0.0f;
+#pragma unroll 4
+        for (int d4 = 0; d4 < D / 4; d4++) {
+            float4 qv[2], kv[4];
+#pragma unroll
+            for (int i = 0; i < 2; i++)
+                qv[i] = *reinterpret_cast<const float4 *>(q_s + (sq + i) * QS + d4 * 4);
+#pragma unroll
+            for (int j = 0; j < 4; j++)
+                kv[j] = *reinterpret_cast<const float4 *>(kb + (kq + 8 * j) * QS + d4 * 4);
+#pragma unroll
+            for (int i = 0; i < 2; i++)
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    float t = sc[i][j];
+                    t = __fadd_rn(t, __fmul_rn(qv[i].x, kv[j].x));
+                    t = __fadd_rn(t, __fmul_rn(qv[i].y, kv[j].y));
+                    t = __fadd_rn(t, __fmul_rn(qv[i].z, kv[j].z));
+                    t = __fadd_rn(t, __fmul_rn(qv[i].w, kv[j].w));
+                    sc[i][j] = t;
+                }
+        }
+        // ---- online softmax (the 8 lanes of a query-vector pair share it)
+        const int t0 = c * PA_KC;
+#pragma unroll
+        for (int i = 0; i < 2; i++) {
+            float mx = -INFINITY;
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                sc[i][j] = (t0 + kq + 8 * j <= pos_s[i]) ? __fmul_rn(sc[i][j], inv_sqrt_d) : -INFINITY;
+                mx = fmaxf(mx, sc[i][j]);
+            }
+#pragma unroll
+            for (int off = 1; off < 8; off <<= 1)
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+            const float m_new = fmaxf(m_run[i], mx);
+            const float corr = (m_run[i] == -INFINITY) ? 0.0f : expf(m_run[i] - m_new);
+            float ps = 0.0f;
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                const float pr = (sc[i][j] == -INFINITY) ? 0.0f : expf(sc[i][j] - m_new);
+                p_s[(kq + 8 * j) * PS + sq + i] = pr;
+                ps += pr;
+            }
+#pragma unroll
+            for (int off = 1; off < 8; off <<= 1)
+                ps += __shfl_xor_sync(0xffffffffu, ps, off);
+            l_run[i] = l_run[i] * corr + ps;
+            m_run[i] = m_new;
+            if ((lane & 7) == 0)
+                c_s[sq + i] = corr;
+        }
+        __syncthreads(); // probabilities and rescales visible
+        // ---- P.V
+        float cr[4];
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+            cr[i] = c_s[oq + i];
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+#pragma unroll
+            for (int j = 0; j < DPT; j++)
+                o[i][j] *= cr[i];
+#pragma unroll 4
+        for (int k = 0; k < PA_KC; k++) {
+            const float4 pv = *reinterpret_cast<const float4 *>(p_s + k * PS + oq);
+            const float pk[4] = {pv.x, pv.y, pv.z, pv.w};
+            float vv[DPT];
+#pragma unroll
+            for (int j = 0; j < DPT; j += 4) {
+                const float4 t = *reinterpret_cast<const float4 *>(vb + k * D + od + j);
+                vv[j] = t.x;
+                vv[j + 1] = t.y;
+                vv[j + 2] = t.z;
+                vv[j + 3] = t.w;
+            }
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+#pragma unroll
+                for (int j = 0; j < DPT; j++)
+                    o[i][j] = fmaf(pk[i], vv[j], o[i][j]);
+        }
+        __syncthreads(); // buffers free for the next loads
+    }
+    // ---- normalise and store: l of query vector qv lives with the score lanes
+    // (sq, sq+1): hand it over through shared memory
+    if ((lane & 7) == 0) {
+        c_s[sq] = l_run[0];
+        c_s[sq + 1] = l_run[1];
+    }
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const int qv = oq + i, r = qv / NREP, h = qv % NREP;
+        if (r >= rows)
+            continue;
+        const float l = c_s[qv];
+        float *dst = ctx + (size_t)(m0 + r) * Hq * D + (size_t)(g * NREP + h) * D + od;
+#pragma unroll
+        for (int j = 0; j < DPT; j += 4)
+            *reinterpret_cast<float4 *>(dst + j) =
+                make_float4(o[i][j] / l, o[i][j + 1] / l, o[i][j + 2] / l, o[i][j + 3] / l);
     }
 }
 
@@ -842,13 +982,13 @@ int prefill_prepare(void)
     LLMRS_PG_VARIANTS(LLMRS_PG_ATTR)
 #undef LLMRS_PG_ATTR
     LLMRS_CUDA_TRY(cudaFuncSetAttribute(prefill_attention_kernel<128, 4>,
-                                        cudaFuncAttributeMaxDynamicSharedMemorySize, PaLayout<128, 4>::BYTES));
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, PaLayout<128>::BYTES));
     LLMRS_CUDA_TRY(cudaFuncSetAttribute(prefill_attention_kernel<128, 8>,
-                                        cudaFuncAttributeMaxDynamicSharedMemorySize, PaLayout<128, 8>::BYTES));
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, PaLayout<128>::BYTES));
     LLMRS_CUDA_TRY(cudaFuncSetAttribute(prefill_attention_kernel<64, 4>,
-                                        cudaFuncAttributeMaxDynamicSharedMemorySize, PaLayout<64, 4>::BYTES));
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, PaLayout<64>::BYTES));
     LLMRS_CUDA_TRY(cudaFuncSetAttribute(prefill_attention_kernel<64, 8>,
-                                        cudaFuncAttributeMaxDynamicSharedMemorySize, PaLayout<64, 8>::BYTES));
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, PaLayout<64>::BYTES));
     return LLMRS_OK;
 }
 
@@ -874,10 +1014,10 @@ int prefill_attention(const float *qkv, const float *kc, const float *vc, float 
 {
     LLMRS_CHECK_ARG(M > 0 && start >= 0 && start + M <= S, "prefill attention: positions out of range");
     const int nrep = Hq / Hkv;
-    const dim3 grid((M + PA_ROWS - 1) / PA_ROWS, Hkv), block(PA_ROWS * 32);
 #define LLMRS_PA_CASE(DD, NR)                                                                              \
     if (D == DD && nrep == NR) {                                                                           \
-        prefill_attention_kernel<DD, NR><<<grid, block, PaLayout<DD, NR>::BYTES, stream>>>(                \
+        const dim3 grid((M + PA_QV / NR - 1) / (PA_QV / NR), Hkv);                                         \
+        prefill_attention_kernel<DD, NR><<<grid, PA_THREADS, PaLayout<DD>::BYTES, stream>>>(               \
             qkv, kc, vc, ctx, M, start, Hq, Hkv, S, inv_sqrt_d);                                           \
         LLMRS_CUDA_TRY(cudaGetLastError());                                                                \
         return LLMRS_OK;                                                                                   \

@@ -13,7 +13,6 @@ namespace llmrs {
 
 constexpr int PG_TILE = 128;      // weight rows (MMA M, TMEM lanes) and token rows (MMA N, TMEM columns) per tile
 constexpr int PG_KSTAGE = 256;    // K elements (8 Q8_0 blocks) per pipeline stage
-constexpr int PG_QUANT_THREADS = 512;
 constexpr int PREFILL_MIN_ROWS = 8; // from this many rows on, M>1 contractions use the tensor cores
 
 // Q8_0 activation rows as the GEMM reads them.  q: [Mpad][K] int8 codes (Q4
