@@ -22,7 +22,10 @@
 //   warps 2..17: TMEM -> registers (32 columns x 32 lanes each), scales, sums;
 //     each warp hands the TMEM buffer back at once and the stage's scales when
 //     it finishes the stage's last block.
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
+
+#include <stdlib.h>
 
 #include <mutex>
 
@@ -503,6 +506,262 @@ __global__ void __launch_bounds__(PG_THREADS, 1)
     }
 }
 
+// ------------------------------------------------- the GEMM, bf16 operands
+// Codes are small integers, exact in bf16, and every partial sum of a block's
+// 32 products is an integer below 2^20, exact in the f32 accumulator: two
+// tcgen05.mma.kind::f16 (K = 16 each) per Q8_0 block leave the block's dot
+// already as a float, so the epilogue is s_w*s_a, isum*(s_w*s_a) and the
+// in-order sum (3 FP32-pipe operations per output and block instead of 4 plus
+// an integer add).  Operands are twice the bytes: a stage is 4 blocks.
+constexpr int PB_BLOCKS = 4;                          // Q8_0 blocks per stage
+constexpr int PB_BOX = PG_TILE * 128;                 // 128 rows x 64 bf16 (one swizzle span)
+struct PbLay {
+    static constexpr int STAGES = 3;
+    static constexpr int OFF_W = 0;                   // 2 swizzled boxes: K 0..63, 64..127 of the stage
+    static constexpr int OFF_A = OFF_W + 2 * PB_BOX;  // 2 swizzled boxes
+    static constexpr int OFF_WS = OFF_A + 2 * PB_BOX; // weight scales [4 blocks][128 rows] f32
+    static constexpr int OFF_AS = OFF_WS + 2048;      // activation scales [4 blocks][128 tokens] f32
+    static constexpr int STAGE = OFF_AS + 2048;       // 68 KB
+    static constexpr int BAR_OFF = STAGES * STAGE;
+    static constexpr int SMEM = BAR_OFF + 256 + 1024;
+    static_assert(SMEM <= 232448, "prefill bf16 GEMM shared memory over the per-block limit");
+};
+
+// kind::f16 instruction descriptor: f32 accumulator, A and B bf16, K-major,
+// M = 128, N = 128
+__host__ __device__ constexpr uint32_t bf16_idesc()
+{
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(PG_TILE >> 3) << 17) | ((uint32_t)(PG_TILE >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc)
+{
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc)
+        : "memory");
+}
+
+// acc[i] += f_i * (sw * sa[i]) for 16 token columns (f_i: the block's dot as float)
+__device__ __forceinline__ void block_sum16_f(float *acc, const uint32_t (&r)[16], float sw, const float *sa)
+{
+    const float2 sw2 = make_float2(sw, sw);
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const float4 a = reinterpret_cast<const float4 *>(sa)[i]; // broadcast
+        const float2 f0 = make_float2(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1]));
+        const float2 f1 = make_float2(__uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3]));
+        const float2 t0 = mul2(f0, mul2(sw2, make_float2(a.x, a.y)));
+        const float2 t1 = mul2(f1, mul2(sw2, make_float2(a.z, a.w)));
+        acc[4 * i] = __fadd_rn(acc[4 * i], t0.x);
+        acc[4 * i + 1] = __fadd_rn(acc[4 * i + 1], t0.y);
+        acc[4 * i + 2] = __fadd_rn(acc[4 * i + 2], t1.x);
+        acc[4 * i + 3] = __fadd_rn(acc[4 * i + 3], t1.y);
+    }
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(PG_THREADS, 1)
+    prefill_gemm_bf16_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap tws,
+                             const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tas,
+                             const PgParams p)
+{
+    using Lay = PbLay;
+    constexpr int S = Lay::STAGES;
+    extern __shared__ uint8_t pg_smem_raw[];
+    uint8_t *sm = align1024(pg_smem_raw);
+    uint64_t *full = reinterpret_cast<uint64_t *>(sm + Lay::BAR_OFF);
+    uint64_t *empty = full + S;
+    uint64_t *tfull = empty + S;
+    uint64_t *tempty = tfull + PG_TBUF;
+    uint64_t *drain = tempty + PG_TBUF;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1 + PG_EPI_WARPS);
+        }
+        for (int b = 0; b < PG_TBUF; b++) {
+            mbar_init(&tfull[b], 1);
+            mbar_init(&tempty[b], PG_EPI_WARPS);
+        }
+        mbar_init(drain, 1);
+        fence_mbar_init();
+    }
+    if (warp == 1)
+        tmem_alloc(tmem_slot, PG_TMEM_COLS);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    const int nks = p.K / (PB_BLOCKS * 32);
+    const int ntiles = p.tiles_n * p.tiles_m;
+    constexpr uint32_t STAGE_TX = 4 * PB_BOX + 2 * PB_BLOCKS * PG_TILE * 4;
+
+    if (warp == 0) {
+        // ---------------------------------------------------------- producer
+        if (lane == 0) {
+            const uint64_t pol_w = policy_evict_first();
+            const uint64_t pol_a = policy_evict_last();
+            uint32_t it = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
+                const int tm = tile % p.tiles_m, tn = tile / p.tiles_m;
+                for (int ks = 0; ks < nks; ks++, it++) {
+                    const int s = it % S;
+                    if (!mbar_wait(&empty[s], ((it / S) & 1) ^ 1, p.err)) {
+                        ok = false;
+                        break;
+                    }
+                    uint8_t *st = sm + s * Lay::STAGE;
+                    mbar_arrive_expect_tx(&full[s], STAGE_TX);
+                    const int k0 = ks * PB_BLOCKS * 32; // element index
+                    tma_load_2d(st + Lay::OFF_W, &tw, k0, tn * PG_TILE, &full[s], pol_w);
+                    tma_load_2d(st + Lay::OFF_W + PB_BOX, &tw, k0 + 64, tn * PG_TILE, &full[s], pol_w);
+                    tma_load_2d(st + Lay::OFF_A, &ta, k0, tm * PG_TILE, &full[s], pol_a);
+                    tma_load_2d(st + Lay::OFF_A + PB_BOX, &ta, k0 + 64, tm * PG_TILE, &full[s], pol_a);
+                    tma_load_2d(st + Lay::OFF_WS, &tws, tn * PG_TILE, ks * PB_BLOCKS, &full[s], pol_w);
+                    tma_load_2d(st + Lay::OFF_AS, &tas, tm * PG_TILE, ks * PB_BLOCKS, &full[s], pol_a);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // --------------------------------------------------------- MMA issuer
+        if (lane == 0) {
+            constexpr uint32_t IDESC = bf16_idesc();
+            uint32_t it = 0, g = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
+                for (int ks = 0; ks < nks; ks++, it++) {
+                    const int s = it % S;
+                    if (!mbar_wait(&full[s], (it / S) & 1, p.err)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t wb = smem_addr(sm + s * Lay::STAGE + Lay::OFF_W);
+                    const uint32_t ab = smem_addr(sm + s * Lay::STAGE + Lay::OFF_A);
+#pragma unroll 1
+                    for (int j = 0; j < PB_BLOCKS; j++, g++) {
+                        const int buf = g % PG_TBUF;
+                        if (!mbar_wait(&tempty[buf], ((g / PG_TBUF) & 1) ^ 1, p.err)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        // block j: 64 bytes at (j % 2) * 64 of box j / 2; two K = 16 halves
+                        const uint32_t koff = (uint32_t)((j >> 1) * PB_BOX + (j & 1) * 64);
+                        const uint32_t d = tmem + (uint32_t)(buf * PG_TILE);
+                        mma_bf16(d, sw128_desc(wb + koff), sw128_desc(ab + koff), IDESC, 0);
+                        mma_bf16(d, sw128_desc(wb + koff + 32), sw128_desc(ab + koff + 32), IDESC, 1);
+                        tc_commit(&tfull[buf]);
+                    }
+                    if (!ok)
+                        break;
+                    tc_commit(&empty[s]);
+                }
+            }
+            tc_commit(drain);
+            mbar_wait(drain, 0, p.err);
+        }
+    } else {
+        // ----------------------------------------------------------- epilogue
+        const int q = warp & 3;
+        const int cg = (warp - 2) >> 2;
+        const int row_l = q * 32 + lane;
+        const uint32_t tl = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(cg * 32);
+        const int my_tiles = (int)blockIdx.x < ntiles ? (ntiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+        const uint32_t total = (uint32_t)my_tiles * (uint32_t)nks * PB_BLOCKS;
+        uint32_t it = 0, g = 0;
+        bool ok = true;
+        uint32_t ra[16], rb[16];
+        auto buf_of = [](uint32_t gg) { return (uint32_t)(gg % PG_TBUF) * PG_TILE; };
+        if (total > 0) {
+            ok = __all_sync(0xffffffffu, mbar_wait(&tfull[0], 0, p.err));
+            tc_fence_after();
+            if (ok)
+                tmem_ld16(tl, ra);
+        }
+        for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
+            const int tm = tile % p.tiles_m, tn = tile / p.tiles_m;
+            float acc[32];
+#pragma unroll
+            for (int i = 0; i < 32; i++)
+                acc[i] = 0.0f;
+            for (int ks = 0; ok && ks < nks; ks++, it++) {
+                const int s = it % S;
+                if (!__all_sync(0xffffffffu, mbar_wait(&full[s], (it / S) & 1, p.err))) {
+                    ok = false;
+                    break;
+                }
+                const uint8_t *st = sm + s * Lay::STAGE;
+                const float *wss = reinterpret_cast<const float *>(st + Lay::OFF_WS) + row_l;
+                const float *sas = reinterpret_cast<const float *>(st + Lay::OFF_AS) + cg * 32;
+#pragma unroll
+                for (int j = 0; j < PB_BLOCKS; j++) {
+                    const float swj = wss[j * PG_TILE];
+                    const float *saj = sas + j * PG_TILE;
+                    tmem_wait_ld(ra);
+                    tmem_ld16(tl + buf_of(g) + 16, rb);
+                    block_sum16_f(acc, ra, swj, saj);
+                    tmem_wait_ld(rb);
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0)
+                        mbar_arrive(&tempty[g % PG_TBUF]);
+                    g++;
+                    if (g < total) {
+                        if (!__all_sync(0xffffffffu, mbar_wait(&tfull[g % PG_TBUF], (g / PG_TBUF) & 1, p.err)))
+                            ok = false;
+                        tc_fence_after();
+                        if (ok)
+                            tmem_ld16(tl + buf_of(g), ra);
+                    }
+                    block_sum16_f(acc + 16, rb, swj, saj + 16);
+                    if (!ok)
+                        break;
+                }
+                __syncwarp();
+                if (lane == 0)
+                    mbar_arrive(&empty[s]);
+            }
+            if (!ok)
+                break;
+            const int n = tn * PG_TILE + row_l;
+            const int m0 = tm * PG_TILE + cg * 32;
+#pragma unroll
+            for (int i = 0; i < 32; i++) {
+                const float v = acc[i];
+                const int m = m0 + i;
+                if (EPI == PEPI_SILU) {
+                    const float up = __shfl_down_sync(0xffffffffu, v, 1);
+                    if (m < p.M && n < p.N && (n & 1) == 0) {
+                        const float silu = __fdiv_rn(v, __fadd_rn(1.0f, expf(-v)));
+                        p.y[(size_t)m * p.ldy + (n >> 1)] = __fmul_rn(silu, up);
+                    }
+                } else if (m < p.M && n < p.N) {
+                    if (EPI == PEPI_RESIDUAL)
+                        p.y[(size_t)m * p.ldy + n] = __fadd_rn(v, p.residual[(size_t)m * p.ldr + n]);
+                    else
+                        p.y[(size_t)m * p.ldy + n] = v;
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        __syncwarp();
+        tc_fence_after();
+        tmem_dealloc(tmem, PG_TMEM_COLS);
+    }
+}
+
 // ------------------------------------------------- per-row activation quantise
 struct PqParams {
     const float *x;
@@ -518,7 +777,7 @@ struct PqParams {
 // One CTA per row: the GEMV's activation prologue (same thread layout, so the
 // RMSNorm sum of squares and every rounding match the batch-1 path bit for
 // bit), then the row's codes and block-major scales go out to global memory.
-template <int WF, int PRO>
+template <int WF, int PRO, bool BF>
 __global__ void __launch_bounds__(PG_QUANT_THREADS) prefill_quant_kernel(const PqParams a)
 {
     extern __shared__ __align__(16) uint8_t qsm[];
@@ -535,14 +794,75 @@ __global__ void __launch_bounds__(PG_QUANT_THREADS) prefill_quant_kernel(const P
     p.err = a.err;
     load_activation<WF, PRO>(p, act, act_s, act_c, red, threadIdx.x, PG_QUANT_THREADS, 1, nullptr);
     __syncthreads();
-    uint4 *dst = reinterpret_cast<uint4 *>(a.q + (size_t)m * K);
-    for (int i = threadIdx.x; i < K / 16; i += PG_QUANT_THREADS)
-        dst[i] = reinterpret_cast<const uint4 *>(act)[i];
+    if (BF) { // codes as bf16 (exact: |code| <= 127), 8 per 16-byte store
+        uint4 *dst = reinterpret_cast<uint4 *>(reinterpret_cast<__nv_bfloat16 *>(a.q) + (size_t)m * K);
+        for (int i = threadIdx.x; i < K / 8; i += PG_QUANT_THREADS) {
+            const uint2 c = reinterpret_cast<const uint2 *>(act)[i];
+            const uint32_t w[2] = {c.x, c.y};
+            uint32_t o[4];
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                const uint32_t src = w[k >> 1] >> (16 * (k & 1));
+                const __nv_bfloat16 lo = __float2bfloat16_rn((float)(int8_t)(src & 0xFF));
+                const __nv_bfloat16 hi = __float2bfloat16_rn((float)(int8_t)((src >> 8) & 0xFF));
+                o[k] = (uint32_t)__bfloat16_as_ushort(lo) | ((uint32_t)__bfloat16_as_ushort(hi) << 16);
+            }
+            dst[i] = make_uint4(o[0], o[1], o[2], o[3]);
+        }
+    } else {
+        uint4 *dst = reinterpret_cast<uint4 *>(a.q + (size_t)m * K);
+        for (int i = threadIdx.x; i < K / 16; i += PG_QUANT_THREADS)
+            dst[i] = reinterpret_cast<const uint4 *>(act)[i];
+    }
     for (int b = threadIdx.x; b < nb; b += PG_QUANT_THREADS) {
         a.s[(size_t)b * a.Mpad + m] = act_s[b];
-        if (WF == 0)
+        if (WF == 0 && !BF)
             a.c[(size_t)b * a.Mpad + m] = PG_MAGIC + act_c[b];
     }
+}
+
+// bf16 copy of one linear: thread = (row n, block b); Q4 codes become
+// nibble - 8 in natural element order; scales f32, block-major [K/32][N]
+template <int WF, int ST>
+__global__ void prefill_to_bf16_kernel(const uint8_t *codes, const void *scales, __nv_bfloat16 *wbf, float *sbf, int N,
+                                       int K)
+{
+    const int nb = K / 32;
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (size_t)N * nb)
+        return;
+    const int n = (int)(i / nb), b = (int)(i % nb);
+    uint32_t o[16];
+    if (WF) {
+        const uint4 *src = reinterpret_cast<const uint4 *>(codes + (size_t)n * K + (size_t)b * 32);
+        const uint4 v0 = src[0], v1 = src[1];
+        const uint32_t w[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+#pragma unroll
+        for (int k = 0; k < 16; k++) {
+            const uint32_t x = w[k >> 1] >> (16 * (k & 1));
+            o[k] = (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn((float)(int8_t)(x & 0xFF))) |
+                   ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn((float)(int8_t)((x >> 8) & 0xFF))) << 16);
+        }
+    } else {
+        const uint4 v = *reinterpret_cast<const uint4 *>(codes + (size_t)n * (K / 2) + (size_t)b * 16);
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int k = 0; k < 16; k++) { // byte k: element 2k (low nibble), 2k+1 (high)
+            const uint32_t byte = (w[k >> 2] >> (8 * (k & 3))) & 0xFF;
+            o[k] = (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn((float)((int)(byte & 15) - 8))) |
+                   ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn((float)((int)(byte >> 4) - 8))) << 16);
+        }
+    }
+    uint4 *dst = reinterpret_cast<uint4 *>(wbf + (size_t)n * K + (size_t)b * 32);
+#pragma unroll
+    for (int k = 0; k < 4; k++)
+        dst[k] = make_uint4(o[4 * k], o[4 * k + 1], o[4 * k + 2], o[4 * k + 3]);
+    float sc;
+    if (ST)
+        sc = reinterpret_cast<const float *>(scales)[(size_t)n * nb + b];
+    else
+        sc = __half2float(reinterpret_cast<const __half *>(scales)[(size_t)n * nb + b]);
+    sbf[(size_t)b * N + n] = sc;
 }
 
 size_t quant_smem(int K) { return (size_t)K + (size_t)(K / 32) * 8 + 32 * 4; }
@@ -851,10 +1171,10 @@ size_t prefill_acts_bytes(int M, int K)
     const size_t Mpad = (size_t)((M + PG_TILE - 1) / PG_TILE) * PG_TILE;
     const size_t nb = (size_t)K / 32;
     auto up = [](size_t b) { return (b + 1023) & ~size_t(1023); };
-    return up(Mpad * K) + up(nb * Mpad * 4) + up(nb * Mpad * 4) + 1024;
+    return up(Mpad * K * 2) + up(nb * Mpad * 4) + up(nb * Mpad * 4) + 1024;
 }
 
-int prefill_acts_init(PrefillActs *a, void *buf, int M, int K, int wf)
+int prefill_acts_init(PrefillActs *a, void *buf, int M, int K, int wf, int bf16)
 {
     LLMRS_CHECK_ARG(a && buf && M > 0 && K > 0 && K % PG_KSTAGE == 0, "prefill acts: bad arguments");
     const int Mpad = (M + PG_TILE - 1) / PG_TILE * PG_TILE;
@@ -862,7 +1182,7 @@ int prefill_acts_init(PrefillActs *a, void *buf, int M, int K, int wf)
     auto up = [](size_t b) { return (b + 1023) & ~size_t(1023); };
     uint8_t *p = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(buf) + 1023) & ~uintptr_t(1023));
     a->q = reinterpret_cast<int8_t *>(p);
-    p += up((size_t)Mpad * K);
+    p += up((size_t)Mpad * K * 2);
     a->s = reinterpret_cast<float *>(p);
     p += up(nb * Mpad * 4);
     a->c = reinterpret_cast<int *>(p);
@@ -870,11 +1190,16 @@ int prefill_acts_init(PrefillActs *a, void *buf, int M, int K, int wf)
     a->Mpad = Mpad;
     a->K = K;
     a->wf = wf;
+    a->bf16 = bf16;
     // rows past M read as zero (TMA fill), so padded columns stay finite
-    LLMRS_TRY(encode_map(&a->tq, a->q, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (size_t)K, (size_t)M, (size_t)K, 128,
-                         PG_TILE, CU_TENSOR_MAP_SWIZZLE_128B));
+    if (bf16)
+        LLMRS_TRY(encode_map(&a->tq, a->q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (size_t)K, (size_t)M, (size_t)K * 2,
+                             64, PG_TILE, CU_TENSOR_MAP_SWIZZLE_128B));
+    else
+        LLMRS_TRY(encode_map(&a->tq, a->q, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (size_t)K, (size_t)M, (size_t)K, 128,
+                             PG_TILE, CU_TENSOR_MAP_SWIZZLE_128B));
     LLMRS_TRY(encode_map(&a->ts, a->s, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (size_t)M, nb, (size_t)Mpad * 4, PG_TILE,
-                         8, CU_TENSOR_MAP_SWIZZLE_NONE));
+                         bf16 ? PB_BLOCKS : 8, CU_TENSOR_MAP_SWIZZLE_NONE));
     LLMRS_TRY(encode_map(&a->tc, a->c, CU_TENSOR_MAP_DATA_TYPE_INT32, 4, (size_t)M, nb, (size_t)Mpad * 4, PG_TILE, 8,
                          CU_TENSOR_MAP_SWIZZLE_NONE));
     return LLMRS_OK;
@@ -905,6 +1230,51 @@ int prefill_weights_init(PrefillWeights *w, const void *codes, const void *scale
     return LLMRS_OK;
 }
 
+size_t prefill_bf16_bytes(int N, int K)
+{
+    auto up = [](size_t b) { return (b + 1023) & ~size_t(1023); };
+    return up((size_t)N * K * 2) + up((size_t)N * (K / 32) * 4) + 1024;
+}
+
+int prefill_weights_to_bf16(PrefillWeights *w, const void *codes, const void *scales, void *buf, cudaStream_t stream)
+{
+    LLMRS_CHECK_ARG(w && w->ok && codes && scales && buf, "prefill bf16 weights: bad arguments");
+    LLMRS_CHECK_ARG(w->N % 4 == 0, "prefill bf16 weights: N=%d not a multiple of 4", w->N);
+    const int N = w->N, K = w->K, nb = K / 32;
+    auto up = [](size_t b) { return (b + 1023) & ~size_t(1023); };
+    uint8_t *p = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(buf) + 1023) & ~uintptr_t(1023));
+    w->wbf = p;
+    w->sbf = reinterpret_cast<float *>(p + up((size_t)N * K * 2));
+    const size_t items = (size_t)N * nb;
+    const unsigned grid = (unsigned)((items + 255) / 256);
+    __nv_bfloat16 *wb = reinterpret_cast<__nv_bfloat16 *>(w->wbf);
+    const uint8_t *c = reinterpret_cast<const uint8_t *>(codes);
+    if (w->wf == 1 && w->st == LLMRS_F32)
+        prefill_to_bf16_kernel<1, 1><<<grid, 256, 0, stream>>>(c, scales, wb, w->sbf, N, K);
+    else if (w->wf == 1)
+        prefill_to_bf16_kernel<1, 0><<<grid, 256, 0, stream>>>(c, scales, wb, w->sbf, N, K);
+    else if (w->st == LLMRS_F32)
+        prefill_to_bf16_kernel<0, 1><<<grid, 256, 0, stream>>>(c, scales, wb, w->sbf, N, K);
+    else
+        prefill_to_bf16_kernel<0, 0><<<grid, 256, 0, stream>>>(c, scales, wb, w->sbf, N, K);
+    LLMRS_CUDA_TRY(cudaGetLastError());
+    LLMRS_TRY(encode_map(&w->tw16, w->wbf, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (size_t)K, (size_t)N, (size_t)K * 2,
+                         64, PG_TILE, CU_TENSOR_MAP_SWIZZLE_128B));
+    LLMRS_TRY(encode_map(&w->ts16, w->sbf, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (size_t)N, (size_t)nb, (size_t)N * 4,
+                         PG_TILE, PB_BLOCKS, CU_TENSOR_MAP_SWIZZLE_NONE));
+    w->bf16 = 1;
+    return LLMRS_OK;
+}
+
+int prefill_use_bf16(void)
+{
+    static const int v = [] {
+        const char *e = getenv("LLMRS_PREFILL_BF16");
+        return e ? (e[0] == '1' ? 1 : 0) : 1;
+    }();
+    return v;
+}
+
 int prefill_quantize(const float *x, int ldx, const float *norm_w, float eps, PrefillActs &a, uint32_t *err,
                      cudaStream_t stream)
 {
@@ -923,16 +1293,21 @@ int prefill_quantize(const float *x, int ldx, const float *norm_w, float eps, Pr
     p.err = err;
     const size_t smem = quant_smem(a.K);
     const dim3 grid(a.M), block(PG_QUANT_THREADS);
-    if (a.wf == 1) {
+    if (a.bf16) { // natural element order for both weight formats
         if (norm_w)
-            prefill_quant_kernel<1, PRO_NORM><<<grid, block, smem, stream>>>(p);
+            prefill_quant_kernel<1, PRO_NORM, true><<<grid, block, smem, stream>>>(p);
         else
-            prefill_quant_kernel<1, PRO_F32><<<grid, block, smem, stream>>>(p);
+            prefill_quant_kernel<1, PRO_F32, true><<<grid, block, smem, stream>>>(p);
+    } else if (a.wf == 1) {
+        if (norm_w)
+            prefill_quant_kernel<1, PRO_NORM, false><<<grid, block, smem, stream>>>(p);
+        else
+            prefill_quant_kernel<1, PRO_F32, false><<<grid, block, smem, stream>>>(p);
     } else {
         if (norm_w)
-            prefill_quant_kernel<0, PRO_NORM><<<grid, block, smem, stream>>>(p);
+            prefill_quant_kernel<0, PRO_NORM, false><<<grid, block, smem, stream>>>(p);
         else
-            prefill_quant_kernel<0, PRO_F32><<<grid, block, smem, stream>>>(p);
+            prefill_quant_kernel<0, PRO_F32, false><<<grid, block, smem, stream>>>(p);
     }
     LLMRS_CUDA_TRY(cudaGetLastError());
     return LLMRS_OK;
@@ -947,7 +1322,8 @@ int prefill_gemm(const PrefillWeights &w, const PrefillActs &a, int epi, float *
                  int ldr, uint32_t *err, int sms, cudaStream_t stream)
 {
     LLMRS_CHECK_ARG(w.ok, "prefill GEMM: weights not on the tensor-core path");
-    LLMRS_CHECK_ARG(a.K == w.K && a.wf == w.wf, "prefill GEMM: activation rows do not match the weights");
+    LLMRS_CHECK_ARG(a.K == w.K && (a.bf16 ? w.bf16 == 1 : a.wf == w.wf),
+                    "prefill GEMM: activation rows do not match the weights");
     LLMRS_CHECK_ARG(y && (epi != PEPI_RESIDUAL || residual) && (epi != PEPI_SILU || w.N % 2 == 0),
                     "prefill GEMM: bad output arguments");
     PgParams p{};
@@ -963,6 +1339,17 @@ int prefill_gemm(const PrefillWeights &w, const PrefillActs &a, int epi, float *
     p.err = err;
     const int tiles = p.tiles_n * p.tiles_m;
     const int grid = tiles < sms ? tiles : sms;
+    if (a.bf16) {
+#define LLMRS_PB_CASE(EPI)                                                                                    \
+    if (epi == EPI) {                                                                                         \
+        prefill_gemm_bf16_kernel<EPI><<<grid, PG_THREADS, PbLay::SMEM, stream>>>(w.tw16, w.ts16, a.tq, a.ts, p); \
+        LLMRS_CUDA_TRY(cudaGetLastError());                                                                   \
+        return LLMRS_OK;                                                                                      \
+    }
+        LLMRS_PB_CASE(PEPI_STORE) LLMRS_PB_CASE(PEPI_RESIDUAL) LLMRS_PB_CASE(PEPI_SILU)
+#undef LLMRS_PB_CASE
+        return fail(LLMRS_ENOTSUP, "prefill GEMM: no bf16 kernel for epi=%d", epi);
+    }
 #define LLMRS_PG_CASE(WF, ST, EPI)                                                                        \
     if (w.wf == WF && (w.st == LLMRS_F32 ? 1 : 0) == ST && epi == EPI) {                                 \
         prefill_gemm_kernel<WF, ST, EPI><<<grid, PG_THREADS, PgLay<WF>::SMEM, stream>>>(w.tw, w.ts, a.tq, a.ts, a.tc, p); \
@@ -981,6 +1368,12 @@ int prefill_prepare(void)
                                         PgLay<WF>::SMEM));
     LLMRS_PG_VARIANTS(LLMRS_PG_ATTR)
 #undef LLMRS_PG_ATTR
+    LLMRS_CUDA_TRY(cudaFuncSetAttribute(prefill_gemm_bf16_kernel<PEPI_STORE>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, PbLay::SMEM));
+    LLMRS_CUDA_TRY(cudaFuncSetAttribute(prefill_gemm_bf16_kernel<PEPI_RESIDUAL>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, PbLay::SMEM));
+    LLMRS_CUDA_TRY(cudaFuncSetAttribute(prefill_gemm_bf16_kernel<PEPI_SILU>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, PbLay::SMEM));
     LLMRS_CUDA_TRY(cudaFuncSetAttribute(prefill_attention_kernel<128, 4>,
                                         cudaFuncAttributeMaxDynamicSharedMemorySize, PaLayout<128>::BYTES));
     LLMRS_CUDA_TRY(cudaFuncSetAttribute(prefill_attention_kernel<128, 8>,

@@ -24,21 +24,37 @@ struct PrefillActs {
     float *s = nullptr;
     int *c = nullptr;
     int M = 0, Mpad = 0, K = 0, wf = 0;
+    int bf16 = 0;         // 1: codes stored as bf16 [Mpad][K] (natural order) for the bf16 tensor-core GEMM
     CUtensorMap tq, ts, tc;
 };
 
-// bytes of device memory one PrefillActs of (M, K) needs
+// bytes of device memory one PrefillActs of (M, K) needs (either code type)
 size_t prefill_acts_bytes(int M, int K);
 // carve a PrefillActs out of buf (prefill_acts_bytes(M, K) bytes, 1024-aligned)
-int prefill_acts_init(PrefillActs *a, void *buf, int M, int K, int wf);
+int prefill_acts_init(PrefillActs *a, void *buf, int M, int K, int wf, int bf16 = 0);
 
 // weight-side tensor maps of one linear (weights never move)
 struct PrefillWeights {
     CUtensorMap tw, ts;
     int wf = 0, st = 0, N = 0, K = 0;
     int ok = 0; // 0: shape not supported by the tensor-core path
+    // bf16 copy for the bf16 tensor-core GEMM: codes (Q4: nibble - 8) as bf16
+    // [N][K] and scales as f32 block-major [K/32][N]
+    void *wbf = nullptr;
+    float *sbf = nullptr;
+    CUtensorMap tw16, ts16;
+    int bf16 = 0;
 };
 int prefill_weights_init(PrefillWeights *w, const void *codes, const void *scales, int N, int K, int wf, int st);
+// bytes the bf16 copy of an (N, K) linear takes
+size_t prefill_bf16_bytes(int N, int K);
+// fill the bf16 copy into buf (prefill_bf16_bytes(N, K) bytes, 1024-aligned) and
+// set its tensor maps
+int prefill_weights_to_bf16(PrefillWeights *w, const void *codes, const void *scales, void *buf,
+                            cudaStream_t stream);
+// which GEMM serves M>1 rows: 1 = bf16 operands (exact integer sums in f32
+// accumulators), 0 = int8 operands (LLMRS_PREFILL_BF16 overrides)
+int prefill_use_bf16(void);
 
 // x rows [M][ldx] -> (RMSNorm with norm_w when non-null) -> Q8_0 rows in a
 int prefill_quantize(const float *x, int ldx, const float *norm_w, float eps, PrefillActs &a, uint32_t *err,

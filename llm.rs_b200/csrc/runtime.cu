@@ -181,6 +181,8 @@ struct llmrs_model {
     float *pf_x = nullptr, *pf_qkv = nullptr, *pf_ctx = nullptr, *pf_act = nullptr;
     int *pf_ids = nullptr;
     void *pf_acts = nullptr;
+    void *pf_bf16 = nullptr; // bf16 copies of every linear (the bf16 prefill GEMM)
+    int pf_bf = 0;
 };
 
 // ================================================================== C ABI
@@ -362,10 +364,14 @@ static int gemv_op(llmrs_ctx *ctx, int wf, const float *a, const void *w, const 
         PrefillWeights pw;
         LLMRS_TRY(prefill_weights_init(&pw, w, scales, n, k, wf, st));
         if (pw.ok) { // tensor cores: per-row Q8_0 quantise, then one GEMM over all rows
+            const int bf = prefill_use_bf16() && n % 4 == 0;
+            const size_t ab = (prefill_acts_bytes(m, k) + 1023) & ~size_t(1023);
             void *scr = nullptr;
-            LLMRS_TRY(ctx_scratch(ctx, prefill_acts_bytes(m, k), &scr));
+            LLMRS_TRY(ctx_scratch(ctx, ab + (bf ? prefill_bf16_bytes(n, k) : 0), &scr));
+            if (bf) // this call's bf16 copy of the weights
+                LLMRS_TRY(prefill_weights_to_bf16(&pw, w, scales, reinterpret_cast<uint8_t *>(scr) + ab, ctx->stream));
             PrefillActs acts;
-            LLMRS_TRY(prefill_acts_init(&acts, scr, m, k, wf));
+            LLMRS_TRY(prefill_acts_init(&acts, scr, m, k, wf, bf));
             LLMRS_TRY(prefill_quantize(a, k, nullptr, 0.0f, acts, ctx->d_err, ctx->stream));
             return prefill_gemm(pw, acts, PEPI_STORE, c, n, nullptr, 0, ctx->d_err, ctx->sms, ctx->stream);
         }
@@ -568,6 +574,8 @@ static void model_free(llmrs_model *m)
         cudaFree(m->step_buf);
     if (m->pf_buf)
         cudaFree(m->pf_buf);
+    if (m->pf_bf16)
+        cudaFree(m->pf_bf16);
     if (m->h_stage)
         cudaFreeHost(m->h_stage);
     delete m;
@@ -749,9 +757,22 @@ static int finish_sync(llmrs_model *m)
     return LLMRS_OK;
 }
 
+// weights changed: the prefill path's bf16 copies are rebuilt on next use
+static void prefill_invalidate(llmrs_model *m)
+{
+    if (m->pf_bf16) {
+        cudaStreamSynchronize(m->ctx->stream);
+        cudaFree(m->pf_bf16);
+    }
+    m->pf_bf16 = nullptr;
+    m->pf_bf = 0;
+    m->pf_weights = -1;
+}
+
 int llmrs_model_init_synthetic(llmrs_model *m, uint64_t seed)
 {
     LLMRS_CHECK_ARG(m, "model is NULL");
+    prefill_invalidate(m);
     LLMRS_CHECK_ARG(m->st == LLMRS_F16 || m->st == LLMRS_F32, "bad scale dtype");
     cudaSetDevice(m->ctx->device);
     cudaStream_t s = m->ctx->stream;
@@ -828,6 +849,8 @@ static int upload_quant(llmrs_model *m, const QW &q, const void *h_codes, const 
 
 int llmrs_model_set_weight(llmrs_model *m, int layer, int which, const void *h_codes, const float *h_scales)
 {
+    if (m)
+        prefill_invalidate(m);
     LLMRS_CHECK_ARG(m && h_codes, "NULL argument");
     if (m->T > 1)
         return fail(LLMRS_ENOTSUP, "set_weight: tensor-parallel models are filled by init_synthetic");
@@ -1335,6 +1358,29 @@ static int prefill_weights_ready(llmrs_model *m, bool *ready)
                 ok = pw[i]->ok;
             }
         }
+        if (ok && prefill_use_bf16()) { // one buffer holds every linear's bf16 copy
+            size_t total = 0;
+            for (int l = 0; l < m->cfg.n_layers; l++) {
+                LayerW &L = m->layers[l];
+                const QW *q[4] = {&L.qkv, &L.o, &L.gate_up, &L.down};
+                for (int i = 0; i < 4; i++)
+                    total += prefill_bf16_bytes(q[i]->n, q[i]->k);
+            }
+            cudaError_t e = cudaMalloc(&m->pf_bf16, total);
+            if (e != cudaSuccess)
+                return fail(LLMRS_ENOMEM, "bf16 prefill weights (%zu bytes): %s", total, cudaGetErrorString(e));
+            uint8_t *b = reinterpret_cast<uint8_t *>(m->pf_bf16);
+            for (int l = 0; l < m->cfg.n_layers; l++) {
+                LayerW &L = m->layers[l];
+                const QW *q[4] = {&L.qkv, &L.o, &L.gate_up, &L.down};
+                PrefillWeights *pw[4] = {&L.p_qkv, &L.p_o, &L.p_gate_up, &L.p_down};
+                for (int i = 0; i < 4; i++) {
+                    LLMRS_TRY(prefill_weights_to_bf16(pw[i], q[i]->w, q[i]->s, b, m->ctx->stream));
+                    b += prefill_bf16_bytes(q[i]->n, q[i]->k);
+                }
+            }
+            m->pf_bf = 1;
+        }
         m->pf_weights = ok;
     }
     *ready = m->pf_weights == 1;
@@ -1382,9 +1428,9 @@ static int prefill_chunk(llmrs_model *m, const int *d_ids, int n, int start)
     const int sms = m->ctx->sms;
     LLMRS_TRY(prefill_embed(m->embed, d_ids, m->pf_x, n, H, m->V, err, s));
     PrefillActs aH, aQ, aF; // one buffer, three row widths (used one after another)
-    LLMRS_TRY(prefill_acts_init(&aH, m->pf_acts, n, H, m->wf));
-    LLMRS_TRY(prefill_acts_init(&aQ, m->pf_acts, n, QD, m->wf));
-    LLMRS_TRY(prefill_acts_init(&aF, m->pf_acts, n, F, m->wf));
+    LLMRS_TRY(prefill_acts_init(&aH, m->pf_acts, n, H, m->wf, m->pf_bf));
+    LLMRS_TRY(prefill_acts_init(&aQ, m->pf_acts, n, QD, m->wf, m->pf_bf));
+    LLMRS_TRY(prefill_acts_init(&aF, m->pf_acts, n, F, m->wf, m->pf_bf));
     const float eps = m->cfg.rms_eps, inv_sqrt_d = 1.0f / sqrtf((float)D);
     for (int l = 0; l < m->cfg.n_layers; l++) {
         LayerW &L = m->layers[l];
