@@ -274,7 +274,7 @@ def run_prefill(L, ctx, args):
     tops = (lin + att) / (ms / 1000.0) / 1e12
     out = {"metric": "prefill tokens/s", "value": round(n / (ms / 1000.0), 1), "unit": "tokens/s",
            "ms": round(ms, 3), "workload": PREFILL["name"], "prompt_tokens": n,
-           "dtype": "q8_0 x q8_0 (int8 tensor-core block dots, f32 block sums)",
+           "dtype": "q8_0 x q8_0 (exact integer block dots on tcgen05 with bf16 operands, f32 block sums)",
            "e2e": {"value": round(n / statistics.median(e2e), 1), "unit": "tokens/s",
                    "h2d_bytes_per_step": 4 * n, "d2h_bytes_per_step": 4 * c["vocab"] + 8},
            "ops_per_prefill": {"linear_int_ops": lin, "attention_f32_flops": att},
@@ -283,7 +283,7 @@ def run_prefill(L, ctx, args):
         out["roofline"] = {"bound": "tensor", "achieved": round(tops, 1), "peak": round(peak, 1), "unit": "TOP/s",
                            "frac": round(tops / peak, 4),
                            "peak_source": "measured here: cuBLASLt int8 GEMM 8192^3 (torch._int_mm)",
-                           "note": "the exact per-32-block f32 epilogue (4 f32 ops per block and output) bounds the "
+                           "note": "the exact per-32-block f32 epilogue (3 f32 ops per block and output) bounds the "
                                    "GEMM, not the tensor pipe"}
     if not args.no_cpu:
         v, cores, t = cpu_prefill_baseline()
