@@ -160,6 +160,17 @@ int llmrs_attention_prefill(llmrs_ctx *ctx, float *d_qkv, float *d_kcache, float
                             const float *d_rope_sin, float *d_out, int n_rows, int n_heads, int n_kv_heads,
                             int head_dim, int max_seq, int start_pos);
 
+/* Next-token sampling of src/main.rs:192-305 on the device, over d_logits[vocab]:
+ * repetition penalty (when repeat_penalty > 1) on each distinct id of
+ * h_recent[n_recent] (the caller passes the last penalty_window ids, at most
+ * 4096), temperature, softmax, then top-p (top_p < 1) or roulette selection.
+ * u in [0, 1) is the uniform draw the reference takes from rng.random::<f32>()
+ * (an OS-seeded generator there; the caller's draw here, so runs repeat).
+ * Probabilities agree with the reference to rounding; ties in p go to the lower
+ * id.  Blocks until *h_token is written. */
+int llmrs_sample(llmrs_ctx *ctx, const float *d_logits, int vocab, const int *h_recent, int n_recent,
+                 float repeat_penalty, float temperature, float top_p, float u, int *h_token);
+
 /* CpuBackend::quantize_row_q8_0 (src/backend/cpu.rs:663-745) for rows of k
  * values: codes [rows][k] and f32 scales [rows][k/32]; bit-exact */
 int llmrs_quantize_row_q8_0(llmrs_ctx *ctx, const float *d_x, int8_t *d_q, float *d_s, int rows, int k);
@@ -235,6 +246,9 @@ int llmrs_prefill(llmrs_model *model, const int *h_ids, int n, int start_pos, fl
  * iters back-to-back prefills with the ids already on the device;
  * LLMRS_ENOTSUP when the prompt/model takes the single-row path */
 int llmrs_model_time_prefill(llmrs_model *model, const int *h_ids, int n, int start_pos, int iters, float *ms_out);
+/* llmrs_sample over the model's last decode/prefill logits (one GPU) */
+int llmrs_model_sample(llmrs_model *model, const int *h_recent, int n_recent, float repeat_penalty, float temperature,
+                       float top_p, float u, int *h_token);
 /* read the last decode/prefill logits (device resident) into h_logits[vocab] */
 int llmrs_model_logits(llmrs_model *model, float *h_logits);
 /* host-only helper: the RoPE cos/sin table the decode step uses, [n_pos][head_dim/2]

@@ -41,7 +41,8 @@ EXPORTS = [
     "llmrs_decode_step", "llmrs_generate", "llmrs_prefill", "llmrs_model_logits", "llmrs_rope_table",
     "llmrs_model_decode_kernel_count", "llmrs_model_time_decode", "llmrs_model_time_prefill",
     "llmrs_model_profile_decode",
-    "llmrs_attention_decode", "llmrs_attention_decode_noalloc", "llmrs_attention_prefill", "llmrs_model_trace_decode",
+    "llmrs_attention_decode", "llmrs_attention_decode_noalloc", "llmrs_attention_prefill",
+    "llmrs_sample", "llmrs_model_sample", "llmrs_model_trace_decode",
     "llmrs_model_tp_region", "llmrs_model_tp_connect", "llmrs_ipc_get_handle", "llmrs_ipc_open_handle",
     "llmrs_ipc_close_handle",
 ]
@@ -129,6 +130,8 @@ def lib():
         "llmrs_model_profile_decode": (ci, [vp, ci, ci, vp, vp, ip]),
         "llmrs_attention_decode": (ci, [vp, vp, vp, vp, vp, vp, vp, ci, ci, ci, ci, ci]),
         "llmrs_attention_prefill": (ci, [vp, vp, vp, vp, vp, vp, vp, ci, ci, ci, ci, ci, ci]),
+        "llmrs_sample": (ci, [vp, vp, ci, vp, ci, cf, cf, cf, cf, ip]),
+        "llmrs_model_sample": (ci, [vp, vp, ci, cf, cf, cf, cf, ip]),
         "llmrs_attention_decode_noalloc": (ci, [vp, vp, vp, vp, vp, vp, vp, ci, ci, ci, ci, ci, vp]),
         "llmrs_model_trace_decode": (ci, [vp, ci, ci, vp, vp, ip]),
         "llmrs_model_tp_region": (ci, [vp, pp, ctypes.POINTER(sz)]),
@@ -361,6 +364,15 @@ class CudaBackend:
                                             out.ptr, n_rows, n_heads, n_kv_heads, head_dim, max_seq, start_pos))
         return out
 
+    def sample(self, logits, recent, repeat_penalty, temperature, top_p, u):
+        """Next-token sampling of src/main.rs:192-305 over device logits (u: the uniform draw)."""
+        r = np.ascontiguousarray(recent, np.int32)
+        tok = ctypes.c_int(-1)
+        check(lib().llmrs_sample(self.ctx.h, logits.ptr, int(logits.nbytes // 4), _ptr(r) if r.size else None,
+                                 int(r.size), float(repeat_penalty), float(temperature), float(top_p), float(u),
+                                 ctypes.byref(tok)))
+        return tok.value
+
     # CpuBackend::quantize_row_q8_0 and Tensor::quantize_q4 (bit-exact)
     def quantize_row_q8_0(self, x):
         k = x.shape[-1]
@@ -455,6 +467,14 @@ class Model:
         check(lib().llmrs_prefill(self.h, _ptr(ids), ids.size, int(start_pos),
                                   None if logits is None else _ptr(logits), ctypes.byref(am)))
         return am.value, logits
+
+    def sample(self, recent, repeat_penalty, temperature, top_p, u):
+        """Sample the next token from the last step's logits (one GPU)."""
+        r = np.ascontiguousarray(recent, np.int32)
+        tok = ctypes.c_int(-1)
+        check(lib().llmrs_model_sample(self.h, _ptr(r) if r.size else None, int(r.size), float(repeat_penalty),
+                                       float(temperature), float(top_p), float(u), ctypes.byref(tok)))
+        return tok.value
 
     def logits(self):
         out = np.zeros(self.vocab_local, np.float32)

@@ -20,6 +20,7 @@
 #include "common.cuh"
 #include "gemv.cuh"
 #include "prefill.cuh"
+#include "sample.cuh"
 #include "step.cuh"
 #include "llmrs_synth.h"
 #include "ops.cuh"
@@ -526,6 +527,16 @@ int llmrs_attention_prefill(llmrs_ctx *ctx, float *d_qkv, float *d_kcache, float
                                   n_kv_heads, head_dim, max_seq, ctx->stream));
     return prefill_attention(d_qkv, d_kcache, d_vcache, d_out, n_rows, start_pos, n_heads, n_kv_heads, head_dim,
                              max_seq, 1.0f / sqrtf((float)head_dim), ctx->stream);
+}
+
+int llmrs_sample(llmrs_ctx *ctx, const float *d_logits, int vocab, const int *h_recent, int n_recent,
+                 float repeat_penalty, float temperature, float top_p, float u, int *h_token)
+{
+    LLMRS_CHECK_ARG(ctx && d_logits && h_token && vocab > 0, "sample: bad arguments");
+    void *scr = nullptr;
+    LLMRS_TRY(ctx_scratch(ctx, sample_scratch_bytes(vocab), &scr));
+    return sample_launch(d_logits, vocab, h_recent, n_recent, repeat_penalty, temperature, top_p, u, scr, h_token,
+                         ctx->stream);
 }
 
 int llmrs_quantize_row_q8_0(llmrs_ctx *ctx, const float *d_x, int8_t *d_q, float *d_s, int rows, int k)
@@ -1559,6 +1570,15 @@ int llmrs_prefill(llmrs_model *m, const int *h_ids, int n, int start_pos, float 
     if (h_argmax)
         *h_argmax = out[0];
     return LLMRS_OK;
+}
+
+int llmrs_model_sample(llmrs_model *m, const int *h_recent, int n_recent, float repeat_penalty, float temperature,
+                       float top_p, float u, int *h_token)
+{
+    LLMRS_CHECK_ARG(m && h_token, "NULL argument");
+    LLMRS_CHECK_ARG(m->T == 1, "sample: a tensor-parallel model holds a vocabulary shard per rank");
+    cudaSetDevice(m->ctx->device);
+    return llmrs_sample(m->ctx, m->logits, m->V, h_recent, n_recent, repeat_penalty, temperature, top_p, u, h_token);
 }
 
 int llmrs_model_logits(llmrs_model *m, float *h_logits)

@@ -11,6 +11,7 @@
  */
 #include "oracle.h"
 
+#include <float.h>
 #include <math.h>
 #include <omp.h>
 #include <stdlib.h>
@@ -389,6 +390,105 @@ int orc_argmax(const float *v, int n)
         if (v[i] > v[best])
             best = i; /* ties keep the lowest index */
     return best;
+}
+
+/* Next-token sampling, src/main.rs:192-305 restated (u: the draw the reference
+ * takes from rng.random::<f32>()).  *margin: how far the walk's running r was
+ * from zero around the pick (small = the draw sits on a boundary). */
+typedef struct {
+    float p;
+    int i;
+} orc_cand;
+
+static int orc_cand_cmp(const void *a, const void *b)
+{
+    const orc_cand *x = (const orc_cand *)a, *y = (const orc_cand *)b;
+    if (x->p > y->p)
+        return -1;
+    if (x->p < y->p)
+        return 1;
+    return x->i < y->i ? -1 : (x->i > y->i); /* the reference's unstable sort leaves ties unordered */
+}
+
+int orc_sample(const float *logits, int V, const int *recent, int n_recent, float penalty, float temperature,
+               float top_p, float u, float *margin)
+{
+    float *l = (float *)malloc((size_t)V * 4), *p = (float *)malloc((size_t)V * 4);
+    memcpy(l, logits, (size_t)V * 4);
+    if (penalty > 1.0f) /* src/main.rs:192-214: each distinct id of the window once */
+        for (int j = 0; j < n_recent; j++) {
+            int id = recent[j], first = id >= 0 && id < V;
+            for (int k = 0; k < j && first; k++)
+                first = recent[k] != id;
+            if (first)
+                l[id] = l[id] < 0.0f ? l[id] * penalty : l[id] / penalty;
+        }
+    if (fabsf(temperature - 1.0f) > 1e-6f) /* src/main.rs:216-222 */
+        for (int i = 0; i < V; i++)
+            l[i] /= temperature;
+    float mx = -FLT_MAX; /* src/main.rs:230-240 */
+    for (int i = 0; i < V; i++)
+        mx = fmaxf(mx, l[i]);
+    for (int i = 0; i < V; i++)
+        p[i] = expf(l[i] - mx);
+    float sum = 0.0f;
+    for (int i = 0; i < V; i++)
+        sum += p[i];
+    for (int i = 0; i < V; i++)
+        p[i] /= sum;
+    int tok = 0;
+    float mg = INFINITY;
+    if (top_p < 1.0f) { /* src/main.rs:246-292 */
+        orc_cand *c = (orc_cand *)malloc((size_t)V * sizeof(orc_cand));
+        int n = 0;
+        for (int i = 0; i < V; i++)
+            if (p[i] > 1e-5f)
+                c[n++] = (orc_cand){p[i], i};
+        if (n == 0)
+            for (int i = 0; i < V; i++)
+                c[n++] = (orc_cand){p[i], i};
+        qsort(c, (size_t)n, sizeof(orc_cand), orc_cand_cmp);
+        float cum = 0.0f;
+        int cut = n - 1;
+        for (int i = 0; i < n; i++) {
+            cum += c[i].p;
+            if (cum > top_p) {
+                cut = i;
+                break;
+            }
+        }
+        float total = 0.0f;
+        for (int i = 0; i <= cut; i++)
+            total += c[i].p;
+        float r = u * total;
+        tok = c[0].i;
+        for (int i = 0; i <= cut; i++) {
+            const float before = r;
+            r -= c[i].p;
+            if (r <= 0.0f) {
+                tok = c[i].i;
+                mg = fminf(before, -r);
+                break;
+            }
+        }
+        free(c);
+    } else { /* src/main.rs:293-305 */
+        float r = u;
+        for (int i = 0; i < V; i++) {
+            const float before = r;
+            r -= p[i];
+            if (r <= 0.0f) {
+                tok = i;
+                mg = fminf(before, -r);
+                break;
+            }
+        }
+    }
+    if (margin)
+        *margin = mg;
+    free(l);
+    free(p);
+    return tok;
 }
 
 float orc_top2_margin(const float *v, int n)

@@ -72,6 +72,8 @@ float *orc_model_vcache(orc_model *m, int layer);
 size_t orc_model_cache_heads(orc_model *m);
 
 int orc_argmax(const float *v, int n);
+int orc_sample(const float *logits, int V, const int *recent, int n_recent, float penalty, float temperature,
+               float top_p, float u, float *margin);
 float orc_top2_margin(const float *v, int n);
 
 /* synthetic generator helpers exposed for tests */

@@ -81,6 +81,7 @@ def lib():
             "orc_model_vcache": (F32P, [vp, ci]),
             "orc_model_cache_heads": (sz, [vp]),
             "orc_argmax": (ci, [F32P, ci]),
+            "orc_sample": (ci, [F32P, ci, I32P, ci, cf, cf, cf, cf, F32P]),
             "orc_top2_margin": (cf, [F32P, ci]),
             "orc_synth_q4": (None, [u64, u32, u32, sz, sz, U8P, F32P]),
             "orc_synth_q8": (None, [u64, u32, u32, sz, sz, I8P, F32P]),
@@ -238,6 +239,16 @@ def scale(x, v):
 def argmax(v):
     v = _f32(v)
     return lib().orc_argmax(_p(v, F32P), v.size)
+
+
+def sample(logits, recent, penalty, temperature, top_p, u):
+    """src/main.rs:192-305 with the caller's uniform draw u: (token, margin)."""
+    v = _f32(logits)
+    r = np.ascontiguousarray(recent, np.int32)
+    m = np.zeros(1, np.float32)
+    t = lib().orc_sample(_p(v, F32P), v.size, _p(r, I32P), r.size, float(penalty), float(temperature), float(top_p),
+                         float(u), _p(m, F32P))
+    return int(t), float(m[0])
 
 
 def top2_margin(v):
