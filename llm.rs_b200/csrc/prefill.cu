@@ -902,9 +902,11 @@ __global__ void prefill_rope_append_kernel(float *qkv, float *kc, float *vc, con
 }
 
 // ------------------------------------------------------------- attention
-// CTA = (RB query rows, KV head g): the RB * NREP = 64 query vectors of the
-// NREP heads of g share every K/V chunk of 32 positions, staged in shared
-// memory with cp.async (double-buffered).  Per chunk:
+// CTA = (RB query rows, KV head g), twice when few cached positions precede
+// the rows: row blocks b and nblk-1-b, so every CTA sees about the same number
+// of causal positions.  The RB * NREP = 64 query vectors of the NREP heads of
+// g share every K/V chunk of 32 positions, staged in shared memory with
+// cp.async (double-buffered).  Per chunk:
 //   scores: thread = 2 query vectors x 4 positions; each score sums q[d]*k[d]
 //     for d = 0..D-1 in order, unfused, then * 1/sqrt(D) -- bit-exact with
 //     the reference's f32 dot (src/backend/cpu.rs:458-551, non-aarch64) --
@@ -941,7 +943,7 @@ template <int D, int NREP>
 __global__ void __launch_bounds__(PA_THREADS, 2) prefill_attention_kernel(const float *qkv, const float *kc,
                                                                           const float *vc, float *ctx, int M,
                                                                           int start, int Hq, int Hkv, int S,
-                                                                          float inv_sqrt_d)
+                                                                          float inv_sqrt_d, int pair)
 {
     using Lay = PaLayout<D>;
     constexpr int RB = PA_QV / NREP; // query rows per CTA
@@ -954,177 +956,186 @@ __global__ void __launch_bounds__(PA_THREADS, 2) prefill_attention_kernel(const 
     float *p_s = reinterpret_cast<float *>(pasm + Lay::P_OFF);
     float *c_s = reinterpret_cast<float *>(pasm + Lay::C_OFF);
     const int tid = threadIdx.x, lane = tid & 31;
-    const int g = blockIdx.y, m0 = blockIdx.x * RB;
+    const int g = blockIdx.y;
     const int ld = (Hq + 2 * Hkv) * D;
-    const int rows = min(RB, M - m0);
-    const int last = start + m0 + rows - 1; // highest position any row of the CTA sees
-    const int nch = last / PA_KC + 1;
-    const float *kg = kc + (size_t)g * S * D;
-    const float *vg = vc + (size_t)g * S * D;
+    // pair: row blocks b and nblk-1-b, a short causal block and a long one
+    const int nblk = (M + RB - 1) / RB;
+    for (int pass = 0; pass < 2; pass++) {
+        const int blk = pass == 0 ? (int)blockIdx.x : nblk - 1 - (int)blockIdx.x;
+        if (pass == 1 && (!pair || blk <= (int)blockIdx.x))
+            break;
+        __syncthreads(); // the previous block's shared-memory reads are done
+        const int m0 = blk * RB;
+        const int rows = min(RB, M - m0);
+        const int last = start + m0 + rows - 1; // highest position any row of the CTA sees
+        const int nch = last / PA_KC + 1;
+        const float *kg = kc + (size_t)g * S * D;
+        const float *vg = vc + (size_t)g * S * D;
 
-    // chunk loader: K rows into padded rows, V rows plain; positions past
-    // `last` are zero-filled (and masked)
-    auto load_chunk = [&](int c, int buf) {
-        const int t0 = c * PA_KC;
-        for (int e = tid; e < PA_KC * D / 4; e += PA_THREADS) {
-            const int r = e / (D / 4), d4 = e % (D / 4);
-            const int t = t0 + r;
-            const bool ok = t <= last;
-            const size_t off = (size_t)(ok ? t : 0) * D + d4 * 4;
-            cp_async16(k_s + (size_t)(buf * PA_KC + r) * QS + d4 * 4, kg + off, ok);
-            cp_async16(v_s + (size_t)(buf * PA_KC + r) * D + d4 * 4, vg + off, ok);
+        // chunk loader: K rows into padded rows, V rows plain; positions past
+        // `last` are zero-filled (and masked)
+        auto load_chunk = [&](int c, int buf) {
+            const int t0 = c * PA_KC;
+            for (int e = tid; e < PA_KC * D / 4; e += PA_THREADS) {
+                const int r = e / (D / 4), d4 = e % (D / 4);
+                const int t = t0 + r;
+                const bool ok = t <= last;
+                const size_t off = (size_t)(ok ? t : 0) * D + d4 * 4;
+                cp_async16(k_s + (size_t)(buf * PA_KC + r) * QS + d4 * 4, kg + off, ok);
+                cp_async16(v_s + (size_t)(buf * PA_KC + r) * D + d4 * 4, vg + off, ok);
+            }
+            cp_async_commit();
+        };
+        load_chunk(0, 0);
+        // query vectors qv = r * NREP + h (row m0 + r, head g*NREP + h)
+        for (int e = tid; e < PA_QV * D / 4; e += PA_THREADS) {
+            const int qv = e / (D / 4), d4 = e % (D / 4);
+            const int r = qv / NREP, h = qv % NREP;
+            float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            if (r < rows)
+                v = *reinterpret_cast<const float4 *>(qkv + (size_t)(m0 + r) * ld + (size_t)(g * NREP + h) * D + d4 * 4);
+            *reinterpret_cast<float4 *>(q_s + qv * QS + d4 * 4) = v;
         }
-        cp_async_commit();
-    };
-    load_chunk(0, 0);
-    // query vectors qv = r * NREP + h (row m0 + r, head g*NREP + h)
-    for (int e = tid; e < PA_QV * D / 4; e += PA_THREADS) {
-        const int qv = e / (D / 4), d4 = e % (D / 4);
-        const int r = qv / NREP, h = qv % NREP;
-        float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-        if (r < rows)
-            v = *reinterpret_cast<const float4 *>(qkv + (size_t)(m0 + r) * ld + (size_t)(g * NREP + h) * D + d4 * 4);
-        *reinterpret_cast<float4 *>(q_s + qv * QS + d4 * 4) = v;
-    }
 
-    // score-phase roles: query vectors sq, sq+1; positions kq, kq+8, kq+16,
-    // kq+24 of the chunk (8 lanes read 8 consecutive K rows: distinct banks)
-    constexpr int PS = Lay::PS;
-    const int sq = (tid >> 3) * 2, kq = tid & 7;
-    int pos_s[2];
-#pragma unroll
-    for (int i = 0; i < 2; i++)
-        pos_s[i] = start + m0 + (sq + i) / NREP;
-    float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.0f, 0.0f};
-    // P.V roles: query vectors oq .. oq+3, dims od .. od+DPT-1
-    const int oq = (tid >> 4) * 4, od = (tid & 15) * DPT;
-    float o[4][DPT];
-#pragma unroll
-    for (int i = 0; i < 4; i++)
-#pragma unroll
-        for (int j = 0; j < DPT; j++)
-            o[i][j] = 0.0f;
-
-    for (int c = 0; c < nch; c++) {
-        const int buf = c & 1;
-        if (c + 1 < nch) {
-            load_chunk(c + 1, buf ^ 1);
-            cp_async_wait_1();
-        } else {
-            cp_async_wait_0();
-        }
-        __syncthreads(); // chunk c (and q_s) visible
-        const float *kb = k_s + (size_t)buf * PA_KC * QS;
-        const float *vb = v_s + (size_t)buf * PA_KC * D;
-        // ---- scores, d in order, unfused
-        float sc[2][4];
+        // score-phase roles: query vectors sq, sq+1; positions kq, kq+8, kq+16,
+        // kq+24 of the chunk (8 lanes read 8 consecutive K rows: distinct banks)
+        constexpr int PS = Lay::PS;
+        const int sq = (tid >> 3) * 2, kq = tid & 7;
+        int pos_s[2];
 #pragma unroll
         for (int i = 0; i < 2; i++)
-#pragma unroll
-            for (int j = 0; j < 4; j++)
-                sc[i][j] = 0.0f;
-#pragma unroll 4
-        for (int d4 = 0; d4 < D / 4; d4++) {
-            float4 qv[2], kv[4];
-#pragma unroll
-            for (int i = 0; i < 2; i++)
-                qv[i] = *reinterpret_cast<const float4 *>(q_s + (sq + i) * QS + d4 * 4);
-#pragma unroll
-            for (int j = 0; j < 4; j++)
-                kv[j] = *reinterpret_cast<const float4 *>(kb + (kq + 8 * j) * QS + d4 * 4);
-#pragma unroll
-            for (int i = 0; i < 2; i++)
-#pragma unroll
-                for (int j = 0; j < 4; j++) {
-                    float t = sc[i][j];
-                    t = __fadd_rn(t, __fmul_rn(qv[i].x, kv[j].x));
-                    t = __fadd_rn(t, __fmul_rn(qv[i].y, kv[j].y));
-                    t = __fadd_rn(t, __fmul_rn(qv[i].z, kv[j].z));
-                    t = __fadd_rn(t, __fmul_rn(qv[i].w, kv[j].w));
-                    sc[i][j] = t;
-                }
-        }
-        // ---- online softmax (the 8 lanes of a query-vector pair share it)
-        const int t0 = c * PA_KC;
-#pragma unroll
-        for (int i = 0; i < 2; i++) {
-            float mx = -INFINITY;
-#pragma unroll
-            for (int j = 0; j < 4; j++) {
-                sc[i][j] = (t0 + kq + 8 * j <= pos_s[i]) ? __fmul_rn(sc[i][j], inv_sqrt_d) : -INFINITY;
-                mx = fmaxf(mx, sc[i][j]);
-            }
-#pragma unroll
-            for (int off = 1; off < 8; off <<= 1)
-                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-            const float m_new = fmaxf(m_run[i], mx);
-            const float corr = (m_run[i] == -INFINITY) ? 0.0f : expf(m_run[i] - m_new);
-            float ps = 0.0f;
-#pragma unroll
-            for (int j = 0; j < 4; j++) {
-                const float pr = (sc[i][j] == -INFINITY) ? 0.0f : expf(sc[i][j] - m_new);
-                p_s[(kq + 8 * j) * PS + sq + i] = pr;
-                ps += pr;
-            }
-#pragma unroll
-            for (int off = 1; off < 8; off <<= 1)
-                ps += __shfl_xor_sync(0xffffffffu, ps, off);
-            l_run[i] = l_run[i] * corr + ps;
-            m_run[i] = m_new;
-            if ((lane & 7) == 0)
-                c_s[sq + i] = corr;
-        }
-        __syncthreads(); // probabilities and rescales visible
-        // ---- P.V
-        float cr[4];
-#pragma unroll
-        for (int i = 0; i < 4; i++)
-            cr[i] = c_s[oq + i];
+            pos_s[i] = start + m0 + (sq + i) / NREP;
+        float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.0f, 0.0f};
+        // P.V roles: query vectors oq .. oq+3, dims od .. od+DPT-1
+        const int oq = (tid >> 4) * 4, od = (tid & 15) * DPT;
+        float o[4][DPT];
 #pragma unroll
         for (int i = 0; i < 4; i++)
 #pragma unroll
             for (int j = 0; j < DPT; j++)
-                o[i][j] *= cr[i];
-#pragma unroll 4
-        for (int k = 0; k < PA_KC; k++) {
-            const float4 pv = *reinterpret_cast<const float4 *>(p_s + k * PS + oq);
-            const float pk[4] = {pv.x, pv.y, pv.z, pv.w};
-            float vv[DPT];
-#pragma unroll
-            for (int j = 0; j < DPT; j += 4) {
-                const float4 t = *reinterpret_cast<const float4 *>(vb + k * D + od + j);
-                vv[j] = t.x;
-                vv[j + 1] = t.y;
-                vv[j + 2] = t.z;
-                vv[j + 3] = t.w;
+                o[i][j] = 0.0f;
+
+        for (int c = 0; c < nch; c++) {
+            const int buf = c & 1;
+            if (c + 1 < nch) {
+                load_chunk(c + 1, buf ^ 1);
+                cp_async_wait_1();
+            } else {
+                cp_async_wait_0();
             }
+            __syncthreads(); // chunk c (and q_s) visible
+            const float *kb = k_s + (size_t)buf * PA_KC * QS;
+            const float *vb = v_s + (size_t)buf * PA_KC * D;
+            // ---- scores, d in order, unfused
+            float sc[2][4];
+#pragma unroll
+            for (int i = 0; i < 2; i++)
+#pragma unroll
+                for (int j = 0; j < 4; j++)
+                    sc[i][j] = 0.0f;
+#pragma unroll 4
+            for (int d4 = 0; d4 < D / 4; d4++) {
+                float4 qv[2], kv[4];
+#pragma unroll
+                for (int i = 0; i < 2; i++)
+                    qv[i] = *reinterpret_cast<const float4 *>(q_s + (sq + i) * QS + d4 * 4);
+#pragma unroll
+                for (int j = 0; j < 4; j++)
+                    kv[j] = *reinterpret_cast<const float4 *>(kb + (kq + 8 * j) * QS + d4 * 4);
+#pragma unroll
+                for (int i = 0; i < 2; i++)
+#pragma unroll
+                    for (int j = 0; j < 4; j++) {
+                        float t = sc[i][j];
+                        t = __fadd_rn(t, __fmul_rn(qv[i].x, kv[j].x));
+                        t = __fadd_rn(t, __fmul_rn(qv[i].y, kv[j].y));
+                        t = __fadd_rn(t, __fmul_rn(qv[i].z, kv[j].z));
+                        t = __fadd_rn(t, __fmul_rn(qv[i].w, kv[j].w));
+                        sc[i][j] = t;
+                    }
+            }
+            // ---- online softmax (the 8 lanes of a query-vector pair share it)
+            const int t0 = c * PA_KC;
+#pragma unroll
+            for (int i = 0; i < 2; i++) {
+                float mx = -INFINITY;
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    sc[i][j] = (t0 + kq + 8 * j <= pos_s[i]) ? __fmul_rn(sc[i][j], inv_sqrt_d) : -INFINITY;
+                    mx = fmaxf(mx, sc[i][j]);
+                }
+#pragma unroll
+                for (int off = 1; off < 8; off <<= 1)
+                    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+                const float m_new = fmaxf(m_run[i], mx);
+                const float corr = (m_run[i] == -INFINITY) ? 0.0f : expf(m_run[i] - m_new);
+                float ps = 0.0f;
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    const float pr = (sc[i][j] == -INFINITY) ? 0.0f : expf(sc[i][j] - m_new);
+                    p_s[(kq + 8 * j) * PS + sq + i] = pr;
+                    ps += pr;
+                }
+#pragma unroll
+                for (int off = 1; off < 8; off <<= 1)
+                    ps += __shfl_xor_sync(0xffffffffu, ps, off);
+                l_run[i] = l_run[i] * corr + ps;
+                m_run[i] = m_new;
+                if ((lane & 7) == 0)
+                    c_s[sq + i] = corr;
+            }
+            __syncthreads(); // probabilities and rescales visible
+            // ---- P.V
+            float cr[4];
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+                cr[i] = c_s[oq + i];
 #pragma unroll
             for (int i = 0; i < 4; i++)
 #pragma unroll
                 for (int j = 0; j < DPT; j++)
-                    o[i][j] = fmaf(pk[i], vv[j], o[i][j]);
+                    o[i][j] *= cr[i];
+#pragma unroll 4
+            for (int k = 0; k < PA_KC; k++) {
+                const float4 pv = *reinterpret_cast<const float4 *>(p_s + k * PS + oq);
+                const float pk[4] = {pv.x, pv.y, pv.z, pv.w};
+                float vv[DPT];
+#pragma unroll
+                for (int j = 0; j < DPT; j += 4) {
+                    const float4 t = *reinterpret_cast<const float4 *>(vb + k * D + od + j);
+                    vv[j] = t.x;
+                    vv[j + 1] = t.y;
+                    vv[j + 2] = t.z;
+                    vv[j + 3] = t.w;
+                }
+#pragma unroll
+                for (int i = 0; i < 4; i++)
+#pragma unroll
+                    for (int j = 0; j < DPT; j++)
+                        o[i][j] = fmaf(pk[i], vv[j], o[i][j]);
+            }
+            __syncthreads(); // buffers free for the next loads
         }
-        __syncthreads(); // buffers free for the next loads
-    }
-    // ---- normalise and store: l of query vector qv lives with the score lanes
-    // (sq, sq+1): hand it over through shared memory
-    if ((lane & 7) == 0) {
-        c_s[sq] = l_run[0];
-        c_s[sq + 1] = l_run[1];
-    }
-    __syncthreads();
+        // ---- normalise and store: l of query vector qv lives with the score lanes
+        // (sq, sq+1): hand it over through shared memory
+        if ((lane & 7) == 0) {
+            c_s[sq] = l_run[0];
+            c_s[sq + 1] = l_run[1];
+        }
+        __syncthreads();
 #pragma unroll
-    for (int i = 0; i < 4; i++) {
-        const int qv = oq + i, r = qv / NREP, h = qv % NREP;
-        if (r >= rows)
-            continue;
-        const float l = c_s[qv];
-        float *dst = ctx + (size_t)(m0 + r) * Hq * D + (size_t)(g * NREP + h) * D + od;
+        for (int i = 0; i < 4; i++) {
+            const int qv = oq + i, r = qv / NREP, h = qv % NREP;
+            if (r >= rows)
+                continue;
+            const float l = c_s[qv];
+            float *dst = ctx + (size_t)(m0 + r) * Hq * D + (size_t)(g * NREP + h) * D + od;
 #pragma unroll
-        for (int j = 0; j < DPT; j += 4)
-            *reinterpret_cast<float4 *>(dst + j) =
-                make_float4(o[i][j] / l, o[i][j + 1] / l, o[i][j + 2] / l, o[i][j + 3] / l);
-    }
+            for (int j = 0; j < DPT; j += 4)
+                *reinterpret_cast<float4 *>(dst + j) =
+                    make_float4(o[i][j] / l, o[i][j + 1] / l, o[i][j + 2] / l, o[i][j + 3] / l);
+        }
+    } // row blocks
 }
 
 // ------------------------------------------------------------- embedding
@@ -1407,11 +1418,15 @@ int prefill_attention(const float *qkv, const float *kc, const float *vc, float 
 {
     LLMRS_CHECK_ARG(M > 0 && start >= 0 && start + M <= S, "prefill attention: positions out of range");
     const int nrep = Hq / Hkv;
+    // pair a short and a long row block per CTA when the causal triangle
+    // dominates (few cached positions before the rows); else one block each
+    const int pair = start < M ? 1 : 0;
 #define LLMRS_PA_CASE(DD, NR)                                                                              \
     if (D == DD && nrep == NR) {                                                                           \
-        const dim3 grid((M + PA_QV / NR - 1) / (PA_QV / NR), Hkv);                                         \
+        const int nblk = (M + PA_QV / NR - 1) / (PA_QV / NR);                                              \
+        const dim3 grid(pair ? (nblk + 1) / 2 : nblk, Hkv);                                                \
         prefill_attention_kernel<DD, NR><<<grid, PA_THREADS, PaLayout<DD>::BYTES, stream>>>(               \
-            qkv, kc, vc, ctx, M, start, Hq, Hkv, S, inv_sqrt_d);                                           \
+            qkv, kc, vc, ctx, M, start, Hq, Hkv, S, inv_sqrt_d, pair);                                     \
         LLMRS_CUDA_TRY(cudaGetLastError());                                                                \
         return LLMRS_OK;                                                                                   \
     }
