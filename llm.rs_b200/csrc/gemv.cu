@@ -168,8 +168,6 @@ __global__ void __launch_bounds__(SIMPLE_THREADS) gemv_simple_kernel(const GemvP
             partial_store(p, row, acc);
         }
     }
-    if (EPI == EPI_PARTIAL)
-        partial_signal(p, threadIdx.x, SIMPLE_THREADS, 1);
     if (EPI == EPI_SILU) {
         // rows (2i, 2i+1) are threads (2i, 2i+1) of this block
         __shared__ float rows_acc[SIMPLE_THREADS];

@@ -33,7 +33,9 @@ constexpr int TP_MAX = 8;
 enum TpCounter : int { TP_CNT_O = 0, TP_CNT_DOWN = 1, TP_CNT_KEY = 2, TP_CNT_N = 4 };
 struct TpLink {
     int rank = 0, size = 1;
-    float *ar[2][TP_MAX] = {};            // [o / down][rank q]: q's receive buffer [size][N], block r from rank r
+    // [o / down][rank q]: q's receive buffer [size][N] of 64-bit words (tag << 32 | f32 bits),
+    // block r written by rank r; a word is valid once it carries the exchange's tag
+    unsigned long long *ar[2][TP_MAX] = {};
     unsigned long long *cnt[TP_MAX] = {}; // [rank q]: q's arrival counters [TP_CNT_N]
     unsigned long long *keys[TP_MAX] = {}; // [rank q]: q's argmax key slots [size]
 };
@@ -80,7 +82,6 @@ struct GemvParams {
     int ar_kind;           // TP_CNT_O / TP_CNT_DOWN
     int ar_index;          // all-reduce instance within the step (layer)
     int ar_per_step;       // instances of this kind per step
-    int ar_arrivals;       // counter increments per instance (ranks x producer CTAs)
     int row_offset;        // EPI_ARGMAX: global index of local row 0
 };
 

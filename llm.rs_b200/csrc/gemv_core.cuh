@@ -237,6 +237,25 @@ __device__ __forceinline__ void quantize_block8(const float (&v)[4], int j, bool
 // fused): 4 rounds with a norm (x and its weights), 8 without; later rounds
 // (larger K) load as they go.
 
+// tag of a tensor-parallel exchange (kind, index) in this step: nonzero and
+// different for every exchange of a kind until 2^32 of them
+__device__ __forceinline__ uint32_t ar_tag(const GemvParams &p)
+{
+    return (uint32_t)(p.state->epoch * (unsigned long long)p.ar_per_step + (unsigned long long)p.ar_index + 1ull);
+}
+
+__device__ __forceinline__ ulonglong2 ld_volatile_u64x2(const unsigned long long *a)
+{
+    ulonglong2 v;
+    asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(v.x), "=l"(v.y) : "l"(a) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void st_volatile_u64(unsigned long long *a, unsigned long long v)
+{
+    asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(a), "l"(v) : "memory");
+}
+
 // dep_wait: this thread has not yet waited for the previous kernel; the loads
 // that do not depend on it (RMSNorm weights) are issued first, then the wait.
 template <int WF, int PRO>
@@ -288,21 +307,46 @@ __device__ __forceinline__ void load_activation(const GemvParams &p, uint32_t *a
         }
         x = p.embed + (size_t)tok * K;
     }
-    const float *part = nullptr; // AR: this rank's receive buffer [size][K]
+    const unsigned long long *part = nullptr; // AR: this rank's receive buffer [size][K]
     int nparts = 0;
+    uint32_t tag = 0;
     if (AR) {
         // the weight stream need not wait for the other ranks
         signal_issued(issued, tid);
         const TpLink *tp = p.tp;
-        if (tid == 0) {
-            const unsigned long long target =
-                ((unsigned long long)p.state->epoch * p.ar_per_step + p.ar_index + 1) * (unsigned long long)p.ar_arrivals;
-            wait_counter(tp->cnt[tp->rank] + p.ar_kind, target, p.err);
-        }
-        named_bar_sync(bar, nthr);
         part = tp->ar[p.ar_kind][tp->rank];
         nparts = tp->size;
+        tag = ar_tag(p);
     }
+    // AR: the 4 partial values of rank q at off, once every word carries this
+    // exchange's tag (each 8-byte word is written whole, so a matching tag
+    // means its value is the one sent); gives up after 5 s
+    auto ll_load4 = [&](int q, size_t off, float (&v)[4]) {
+        const unsigned long long *src = part + (size_t)q * K + off;
+        uint64_t t0 = 0;
+        for (uint32_t spin = 0;; spin++) {
+            const ulonglong2 a = ld_volatile_u64x2(src), c = ld_volatile_u64x2(src + 2);
+            if ((uint32_t)(a.x >> 32) == tag && (uint32_t)(a.y >> 32) == tag && (uint32_t)(c.x >> 32) == tag &&
+                (uint32_t)(c.y >> 32) == tag) {
+                v[0] = __uint_as_float((uint32_t)a.x);
+                v[1] = __uint_as_float((uint32_t)a.y);
+                v[2] = __uint_as_float((uint32_t)c.x);
+                v[3] = __uint_as_float((uint32_t)c.y);
+                return;
+            }
+            if ((spin & 63u) == 0u) {
+                const uint64_t now = globaltimer_ns();
+                if (spin == 0u)
+                    t0 = now;
+                else if (now - t0 > 5000000000ull ||
+                         *reinterpret_cast<volatile uint32_t *>(p.err) == DEV_ERR_PEER_TIMEOUT) {
+                    atomicCAS(p.err, 0u, (uint32_t)DEV_ERR_PEER_TIMEOUT);
+                    v[0] = v[1] = v[2] = v[3] = 0.0f;
+                    return;
+                }
+            }
+        }
+    };
     // the 4 values of block b this lane holds: x, or (AR) the ranks' partial
     // sums in rank order, then + x
     auto load4 = [&](int b, float (&u)[4]) {
@@ -312,19 +356,18 @@ __device__ __forceinline__ void load_activation(const GemvParams &p, uint32_t *a
         u[1] = t.y;
         u[2] = t.z;
         u[3] = t.w;
-        if (AR) {
-            float4 s = __ldcg(reinterpret_cast<const float4 *>(part + off));
+        if (AR) { // the ranks' partial sums in rank order, then + x
+            float s[4], w[4];
+            ll_load4(0, off, s);
             for (int q = 1; q < nparts; q++) {
-                const float4 w = __ldcg(reinterpret_cast<const float4 *>(part + (size_t)q * K + off));
-                s.x = __fadd_rn(s.x, w.x);
-                s.y = __fadd_rn(s.y, w.y);
-                s.z = __fadd_rn(s.z, w.z);
-                s.w = __fadd_rn(s.w, w.w);
+                ll_load4(q, off, w);
+#pragma unroll
+                for (int i = 0; i < 4; i++)
+                    s[i] = __fadd_rn(s[i], w[i]);
             }
-            u[0] = __fadd_rn(s.x, u[0]);
-            u[1] = __fadd_rn(s.y, u[1]);
-            u[2] = __fadd_rn(s.z, u[2]);
-            u[3] = __fadd_rn(s.w, u[3]);
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+                u[i] = __fadd_rn(s[i], u[i]);
         }
     };
     auto load4w = [&](int b, float (&u)[4]) {
@@ -430,25 +473,15 @@ __device__ __forceinline__ void load_activation(const GemvParams &p, uint32_t *a
     }
 }
 
-// Tensor parallel: this CTA's partial rows are in every rank's buffer; count
-// the CTA in on every rank.  The barrier orders every thread's stores before
-// thread 0's system-scope fence (cumulativity), which orders them before the
-// counter increments the other ranks acquire.
-__device__ __forceinline__ void partial_signal(const GemvParams &p, int tid, int nthr, int bar)
-{
-    named_bar_sync(bar, nthr);
-    if (tid == 0) {
-        __threadfence_system();
-        for (int q = 0; q < p.tp->size; q++)
-            atomicAdd_system(p.tp->cnt[q] + p.ar_kind, 1ull);
-    }
-}
-
+// Tensor parallel: this row's partial sum goes to every rank's buffer as one
+// 64-bit word carrying the exchange's tag, so a reader knows the value has
+// arrived without a fence or a counter (a word is written whole).
 __device__ __forceinline__ void partial_store(const GemvParams &p, int row, float acc)
 {
+    const unsigned long long w = ((unsigned long long)ar_tag(p) << 32) | __float_as_uint(acc);
     const size_t off = (size_t)p.tp->rank * p.N + row;
     for (int q = 0; q < p.tp->size; q++)
-        p.tp->ar[p.ar_kind][q][off] = acc;
+        st_volatile_u64(p.tp->ar[p.ar_kind][q] + off, w);
 }
 
 // ------------------------------------------------------------- block dots
@@ -909,8 +942,6 @@ __device__ __forceinline__ void gemv_consume(const GemvParams &p, const GemvWork
     // every consumer thread advances the op-start parities identically
     cpar ^= gemv_stage_use_parity(w, sm.S);
     lpar ^= gemv_link_parity(w);
-    if (EPI == EPI_PARTIAL)
-        partial_signal(p, ctid, PRO_THREADS, 1);
     if (EPI == EPI_ARGMAX)
         argmax_finalize(p, best, ctid, PRO_THREADS, 1);
 }

@@ -733,8 +733,8 @@ int llmrs_model_create(llmrs_ctx *ctx, const llmrs_config *cfg, llmrs_model **ou
         // communication region: partials [T][H] for o_proj and down_proj, keys [T], counters
         auto up = [](size_t v) { return (v + 255) & ~size_t(255); };
         m->tp_off_o = 0;
-        m->tp_off_d = up((size_t)m->T * H * 4);
-        m->tp_off_keys = m->tp_off_d + up((size_t)m->T * H * 4);
+        m->tp_off_d = up((size_t)m->T * H * 8);
+        m->tp_off_keys = m->tp_off_d + up((size_t)m->T * H * 8);
         m->tp_off_cnt = m->tp_off_keys + up((size_t)m->T * 8);
         m->tp_bytes = m->tp_off_cnt + up((size_t)TP_CNT_N * 8);
         e = cudaMalloc(&m->tp_region, m->tp_bytes);
@@ -1013,7 +1013,6 @@ static void build_ops(llmrs_model *m, std::vector<HostOp> &ops, unsigned long lo
         g.ar_kind = kind;
         g.ar_index = index;
         g.ar_per_step = L_n;
-        g.ar_arrivals = m->T * (grid ? grid : gemv_grid(producer.plan));
         g.x = x_in;
         g.x_out = x_out;
     };
@@ -1090,9 +1089,12 @@ static void build_ops(llmrs_model *m, std::vector<HostOp> &ops, unsigned long lo
         o.x = m->ctxv;
         o.y = m->x;
         o.residual = m->x;
-        if (tp) {
+        if (tp) { // producer of exchange (o, l): its tag comes from the step's epoch
             o.tp = m->d_tp;
+            o.state = m->state;
             o.ar_kind = TP_CNT_O;
+            o.ar_index = l;
+            o.ar_per_step = L_n;
         }
         push_gemv(2, L.o, o, PRO_F32, tp ? EPI_PARTIAL : EPI_RESIDUAL);
         // (4) post RMSNorm + gate_up + SiLU*up (src/core/layer.rs:37-89)
@@ -1121,7 +1123,10 @@ static void build_ops(llmrs_model *m, std::vector<HostOp> &ops, unsigned long lo
         d.residual = m->x;
         if (tp) {
             d.tp = m->d_tp;
+            d.state = m->state;
             d.ar_kind = TP_CNT_DOWN;
+            d.ar_index = l;
+            d.ar_per_step = L_n;
         }
         push_gemv(4, L.down, d, PRO_F32, tp ? EPI_PARTIAL : EPI_RESIDUAL);
     }
@@ -1712,8 +1717,8 @@ int llmrs_model_tp_connect(llmrs_model *m, void *const *regions)
     for (int q = 0; q < m->T; q++) {
         LLMRS_CHECK_ARG(regions[q] != nullptr, "region of rank %d is NULL", q);
         uint8_t *b = reinterpret_cast<uint8_t *>(regions[q]);
-        h.ar[TP_CNT_O][q] = reinterpret_cast<float *>(b + m->tp_off_o);
-        h.ar[TP_CNT_DOWN][q] = reinterpret_cast<float *>(b + m->tp_off_d);
+        h.ar[TP_CNT_O][q] = reinterpret_cast<unsigned long long *>(b + m->tp_off_o);
+        h.ar[TP_CNT_DOWN][q] = reinterpret_cast<unsigned long long *>(b + m->tp_off_d);
         h.keys[q] = reinterpret_cast<unsigned long long *>(b + m->tp_off_keys);
         h.cnt[q] = reinterpret_cast<unsigned long long *>(b + m->tp_off_cnt);
     }
