@@ -59,7 +59,7 @@ def oracle_run(orc, cfg, seed, prompt, n_decode, kv):
     return out, forced
 
 
-@pytest.mark.parametrize("world,shape", [(2, "small"), (2, "8b2")])
+@pytest.mark.parametrize("world,shape", [(2, "small"), (2, "8b2"), (4, "8b2"), (8, "8b2")])
 def test_tensor_parallel_decode_matches_oracle(orc, world, shape):
     if n_gpus() < world:
         pytest.skip("needs %d GPUs" % world)
