@@ -1,8 +1,9 @@
-"""Tensor-parallel decode on 2 GPUs (one process per GPU, shards connected
-over CUDA IPC / NVLink) against the single-device CPU oracle.  The o_proj and
-down_proj sums are split across ranks and added in rank order, so logits agree
-to rounding (same bounds as the single-GPU parity tests); greedy tokens must
-match (teacher-forced).  Skipped on boxes with fewer than 2 GPUs."""
+"""Tensor-parallel decode on 2, 4 and 8 GPUs (one process per GPU, shards
+connected over CUDA IPC / NVLink) against the single-device CPU oracle.  The
+o_proj and down_proj sums are split across ranks and added in rank order, so
+logits agree to rounding (same bounds as the single-GPU parity tests); greedy
+tokens must match (teacher-forced).  Each case is skipped on boxes with fewer
+GPUs than its ranks."""
 import json
 import os
 import socket
