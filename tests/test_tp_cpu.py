@@ -1,4 +1,4 @@
-"""The N > 1 path on CPU: two gloo ranks (tests/tp_cpu_worker.py) check the
+"""The N > 1 path on CPU: two and four gloo ranks (tests/tp_cpu_worker.py) check the
 IPC-handle exchange helper and that the tensor-parallel partition of the model
 -- the one the CUDA path implements -- reproduces the unsharded oracle (logits
 to rounding, greedy tokens identical)."""
@@ -9,6 +9,7 @@ import subprocess
 import sys
 
 import numpy as np
+import pytest
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
@@ -19,9 +20,14 @@ def free_port():
         return s.getsockname()[1]
 
 
-def test_tensor_parallel_partition_two_gloo_ranks(orc):
-    cfg = dict(n_layers=2, hidden=256, n_heads=8, n_kv_heads=2, head_dim=32, ffn=512, vocab=1000, max_seq=16,
-               rms_eps=1e-5, rope_theta=500000.0, weight_format=0, tied_embeddings=1)
+CFG2 = dict(n_layers=2, hidden=256, n_heads=8, n_kv_heads=2, head_dim=32, ffn=512, vocab=1000, max_seq=16,
+            rms_eps=1e-5, rope_theta=500000.0, weight_format=0, tied_embeddings=1)
+# four ranks: one KV head and four query heads each
+CFG4 = dict(CFG2, hidden=512, n_heads=16, n_kv_heads=4, ffn=1024)
+
+
+@pytest.mark.parametrize("world,cfg", [(2, CFG2), (4, CFG4)])
+def test_tensor_parallel_partition_gloo_ranks(orc, world, cfg):
     seed = 31
     om = orc.Model(cfg)
     om.init_synthetic(seed)
@@ -29,7 +35,7 @@ def test_tensor_parallel_partition_two_gloo_ranks(orc):
     ref = [om.forward([t], i) for i, t in enumerate(tokens)]
     spec = dict(cfg=cfg, seed=seed, tokens=tokens)
     env = dict(os.environ, CUDA_VISIBLE_DEVICES="")
-    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2",
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", str(world),
            "--master-addr", "127.0.0.1", "--master-port", str(free_port()),
            os.path.join(ROOT, "tests", "tp_cpu_worker.py"), json.dumps(spec)]
     r = subprocess.run(cmd, capture_output=True, text=True, timeout=300, env=env)
