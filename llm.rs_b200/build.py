@@ -15,7 +15,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libllmrs_cuda.so")
-SOURCES = ["step.cu", "prefill.cu", "sample.cu", "gemv.cu", "attention.cu", "ops.cu", "runtime.cu"]
+SOURCES = ["prefill.cu", "sample.cu", "gemv.cu", "attention.cu", "ops.cu", "runtime.cu"]
 
 
 def nvcc():

@@ -1,7 +1,6 @@
-// attention_core.cuh - device pieces of batch-1 decode attention shared by the
-// one-kernel path (attention.cu) and the persistent decode-step kernel
-// (step.cu): the swizzled K-box layout, table-driven RoPE, and the per-warp
-// chunk step (bit-exact scores, online softmax, V accumulation).
+// attention_core.cuh - device pieces of batch-1 decode attention (attention.cu):
+// the swizzled K-box layout, table-driven RoPE, and the per-warp chunk step
+// (bit-exact scores, online softmax, V accumulation).
 #pragma once
 
 #include "common.cuh"

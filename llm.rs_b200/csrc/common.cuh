@@ -51,8 +51,6 @@ enum : uint32_t {
     DEV_ERR_PEER_TIMEOUT = 2,
     DEV_ERR_BAD_TOKEN = 3,
     DEV_ERR_BAD_POS = 4,
-    DEV_ERR_BAD_OP = 5,       // decode-step kernel met an op it was not built for
-    DEV_ERR_STEP_TIMEOUT = 6, // decode-step kernel: an op's input never completed
 };
 
 // launch a kernel; with pdl=true it may begin before the previous kernel in the
@@ -193,7 +191,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint32
         return true;
     if (err) { // after one timeout in this launch, later waits give up at once
         const uint32_t e = *reinterpret_cast<volatile uint32_t *>(err);
-        if (e == DEV_ERR_MBAR_TIMEOUT || e == DEV_ERR_PEER_TIMEOUT || e == DEV_ERR_STEP_TIMEOUT)
+        if (e == DEV_ERR_MBAR_TIMEOUT || e == DEV_ERR_PEER_TIMEOUT)
             return false;
     }
     uint64_t t0 = globaltimer_ns();

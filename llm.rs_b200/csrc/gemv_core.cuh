@@ -1,8 +1,7 @@
 // gemv_core.cuh - device side of the batch-1 Q4_0 / Q8_0 GEMV: shared-memory
 // layout, activation prologue, block dots, the producer (weight stream) and
-// the consumer (dp4a products, in-order row sums, epilogues).  Used by the
-// one-kernel-per-GEMV path (gemv.cu) and by the persistent decode-step kernel
-// (step.cu).  Arithmetic: see gemv.cu.
+// the consumer (dp4a products, in-order row sums, epilogues), used by
+// gemv.cu.  Arithmetic: see gemv.cu.
 #pragma once
 
 #include <cudaTypedefs.h>

@@ -21,7 +21,6 @@
 #include "gemv.cuh"
 #include "prefill.cuh"
 #include "sample.cuh"
-#include "step.cuh"
 #include "llmrs_synth.h"
 #include "ops.cuh"
 
@@ -154,13 +153,6 @@ struct llmrs_model {
     size_t tp_bytes = 0, tp_off_o = 0, tp_off_d = 0, tp_off_keys = 0, tp_off_cnt = 0;
     TpLink *d_tp = nullptr;
     bool tp_connected = false;
-    // the persistent decode-step kernel (op list in device memory)
-    bool step_tried = false;
-    void *step_buf = nullptr;
-    StepOp *step_ops = nullptr;
-    unsigned long long *step_done = nullptr;
-    int step_n_ops = 0, step_stages = 0, step_kmax = 0, step_grid = 0;
-    size_t step_smem = 0;
     unsigned int *att_counter = nullptr;
     StepState *state = nullptr;
     int *token_log = nullptr;
@@ -237,8 +229,6 @@ int llmrs_ctx_create(int device, llmrs_ctx **out)
     int rc = gemv_prepare();
     if (rc == LLMRS_OK)
         rc = attention_prepare();
-    if (rc == LLMRS_OK)
-        rc = step_prepare();
     if (rc == LLMRS_OK)
         rc = prefill_prepare();
     if (rc != LLMRS_OK) {
@@ -581,8 +571,6 @@ static void model_free(llmrs_model *m)
         cudaFree(m->arena.base);
     if (m->tp_region)
         cudaFree(m->tp_region);
-    if (m->step_buf)
-        cudaFree(m->step_buf);
     if (m->pf_buf)
         cudaFree(m->pf_buf);
     if (m->pf_bf16)
@@ -976,10 +964,9 @@ struct KernelTimer {
     }
 };
 
-// One op of a decode step, as both execution paths see it: a GEMV over a
-// weight matrix (with its prologue / epilogue variant) or decode attention.
-// wait_op: the op whose whole output this op reads (-1: none, or an
-// all-reduce prologue that waits on the ranks' counters itself).
+// One op of a decode step: a GEMV over a weight matrix (with its prologue /
+// epilogue variant) or decode attention.
+enum HostOpKind : int { OP_GEMV = 0, OP_ATTN = 1 };
 struct HostOp {
     int kind = OP_GEMV;
     int trace_kind = 0; // KERNEL kind of profile_decode / trace_decode
@@ -987,13 +974,10 @@ struct HostOp {
     GemvParams g{};
     int pro = PRO_F32, epi = EPI_STORE;
     AttnParams a{};
-    int wait_op = -1;
 };
 
-// The decode step (src/core/model.rs:17-49 for a 1-token chunk) as an op
-// list.  grid: CTAs every GEMV launches with when all ops run in one
-// persistent kernel (0: each GEMV's own plan grid).
-static void build_ops(llmrs_model *m, std::vector<HostOp> &ops, unsigned long long *trace, int grid)
+// The decode step (src/core/model.rs:17-49 for a 1-token chunk) as an op list.
+static void build_ops(llmrs_model *m, std::vector<HostOp> &ops, unsigned long long *trace)
 {
     ops.clear();
     int slot = 0;
@@ -1026,7 +1010,6 @@ static void build_ops(llmrs_model *m, std::vector<HostOp> &ops, unsigned long lo
         o.g.trace_slot = slot++;
         o.pro = pro;
         o.epi = epi;
-        o.wait_op = (ops.empty() || pro == PRO_AR_NORM) ? -1 : (int)ops.size() - 1;
         ops.push_back(o);
     };
     for (int l = 0; l < L_n; l++) {
@@ -1077,7 +1060,6 @@ static void build_ops(llmrs_model *m, std::vector<HostOp> &ops, unsigned long lo
         a.inv_sqrt_d = 1.0f / sqrtf((float)m->D);
         a.trace = trace;
         a.trace_slot = slot++;
-        at.wait_op = (int)ops.size() - 1;
         ops.push_back(at);
         // (3) o_proj + residual (src/core/layer.rs:332, 386)
         GemvParams o{};
@@ -1160,7 +1142,7 @@ static int enqueue_step(llmrs_model *m, cudaStream_t s, KernelTimer *kt = nullpt
     // programmatic overlap, so each event pair times exactly one kernel
     const bool overlap = kt == nullptr;
     std::vector<HostOp> ops;
-    build_ops(m, ops, trace, 0);
+    build_ops(m, ops, trace);
     for (size_t i = 0; i < ops.size(); i++) {
         const HostOp &o = ops[i];
         if (kt)
@@ -1175,95 +1157,12 @@ static int enqueue_step(llmrs_model *m, cudaStream_t s, KernelTimer *kt = nullpt
     return LLMRS_OK;
 }
 
-// The persistent decode-step kernel: upload the op list once per model.
-static bool step_kernel_enabled(void)
-{
-    static const bool on = [] {
-        const char *e = getenv("LLMRS_STEP_KERNEL");
-        return e && e[0] == '1';
-    }();
-    return on;
-}
-
-static int setup_step_kernel(llmrs_model *m)
-{
-    if (m->step_tried)
-        return LLMRS_OK;
-    m->step_tried = true;
-    if (!step_kernel_enabled())
-        return LLMRS_OK;
-    const int kmax = std::max(std::max(m->H, m->F), m->Hq * m->D);
-    int stages = 0;
-    const size_t smem = step_smem_bytes(m->wf, m->st, m->lm_head.st, m->D, m->Hq / m->Hkv, m->T > 1, kmax, &stages);
-    if (smem == 0)
-        return LLMRS_OK; // no kernel built for this shape: one kernel per op
-    const int G = m->ctx->sms;
-    std::vector<HostOp> ops;
-    build_ops(m, ops, nullptr, G);
-    std::vector<StepOp> h(ops.size());
-    for (size_t i = 0; i < ops.size(); i++) {
-        StepOp &so = h[i];
-        memset(&so, 0, sizeof(so));
-        const HostOp &o = ops[i];
-        so.kind = o.kind;
-        so.wait_op = o.wait_op;
-        if (o.kind == OP_GEMV) {
-            const GemvPlan &pl = o.q->plan;
-            if (!pl.fast)
-                return LLMRS_OK; // a shape only the fallback GEMV handles: one kernel per op
-            so.tw = pl.tw;
-            so.ts = pl.ts;
-            so.g = o.g;
-            so.g.n_stages = stages;
-            so.g.n_pre = -1;
-            so.g.box_rows = pl.box_rows;
-            so.g.rows_per_cta = pl.rows_per_cta;
-            so.pro = o.pro;
-            so.epi = o.epi;
-            so.wf = pl.wf;
-            so.st = pl.st;
-            if (pl.grid > G)
-                return LLMRS_OK;
-        } else {
-            so.a = o.a;
-            LLMRS_TRY(encode_k_map(&so.a.tk, o.a.kc, o.a.n_kv * o.a.max_seq, o.a.head_dim, STEP_ATTN_ROWS));
-            if (o.a.n_splits * o.a.n_kv > G)
-                return LLMRS_OK;
-        }
-    }
-    const size_t bytes = h.size() * sizeof(StepOp) + (ops.size() + 1) * 8; // + the launch counter
-    void *buf = nullptr;
-    LLMRS_CUDA_TRY(cudaMalloc(&buf, bytes));
-    m->step_buf = buf;
-    m->step_ops = reinterpret_cast<StepOp *>(buf);
-    m->step_done = reinterpret_cast<unsigned long long *>(reinterpret_cast<uint8_t *>(buf) + h.size() * sizeof(StepOp));
-    cudaStream_t s = m->ctx->stream;
-    LLMRS_CUDA_TRY(cudaMemcpyAsync(m->step_ops, h.data(), h.size() * sizeof(StepOp), cudaMemcpyHostToDevice, s));
-    LLMRS_CUDA_TRY(cudaMemsetAsync(m->step_done, 0, (ops.size() + 1) * 8, s));
-    LLMRS_CUDA_TRY(cudaStreamSynchronize(s));
-    m->step_n_ops = (int)ops.size();
-    m->step_smem = smem;
-    m->step_stages = stages;
-    m->step_kmax = kmax;
-    m->step_grid = G;
-    return LLMRS_OK;
-}
-
-static int launch_step_kernel(llmrs_model *m, cudaStream_t s, unsigned long long *trace)
-{
-    return step_launch(m->wf, m->st, m->lm_head.st, m->D, m->Hq / m->Hkv, m->T > 1, m->step_kmax, m->step_stages,
-                       m->step_smem,
-                       m->step_grid, m->step_ops, m->step_n_ops, m->step_done, m->state, &m->state->err, trace, s);
-}
-
 static int capture_step(llmrs_model *m, cudaGraphExec_t *out, unsigned long long *trace)
 {
     cudaStream_t s = m->ctx->stream;
     cudaGraph_t g = nullptr;
-    LLMRS_TRY(setup_step_kernel(m));
-    const bool one_kernel = m->step_ops != nullptr;
     LLMRS_CUDA_TRY(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
-    int rc = one_kernel ? launch_step_kernel(m, s, trace) : enqueue_step(m, s, nullptr, trace);
+    int rc = enqueue_step(m, s, nullptr, trace);
     cudaError_t e = cudaStreamEndCapture(s, &g);
     if (rc != LLMRS_OK) {
         if (g)
@@ -1297,7 +1196,7 @@ static int check_state_err(llmrs_model *m, uint32_t e)
         return LLMRS_OK;
     cudaMemsetAsync(&m->state->err, 0, 4, m->ctx->stream);
     cudaStreamSynchronize(m->ctx->stream);
-    if (e == DEV_ERR_MBAR_TIMEOUT || e == DEV_ERR_PEER_TIMEOUT || e == DEV_ERR_STEP_TIMEOUT)
+    if (e == DEV_ERR_MBAR_TIMEOUT || e == DEV_ERR_PEER_TIMEOUT)
         return fail(LLMRS_ETIMEDOUT, "decode step: device wait timed out (code %u)", e);
     return fail(LLMRS_EDEVICE, "decode step: device error word %u (%s)", e,
                 e == DEV_ERR_BAD_TOKEN ? "token id out of range" : (e == DEV_ERR_BAD_POS ? "position out of range" : "?"));
