@@ -3,23 +3,35 @@
 roofline, the end-to-end rate through the C ABI, and the CPU oracle baseline.
 
 python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                [--workload 8b|1b|70b] [--no-prefill] [--no-cpu]
-
-On one GPU the line also carries "prefill": config 4 (the 8B shape with Q8_0
-linears), a 512-token prompt through the tensor-core prefill path, timed with
-CUDA events over back-to-back prefills (ids resident), plus its end-to-end
-rate through llmrs_prefill and the CPU oracle's prefill rate.
+                [--workload 8b|1b|70b] [--no-extra] [--no-prefill] [--no-cpu]
 
 One "step" = one greedy decode token through every layer + LM head.  Inputs
 (weights 4.2 GB, KV 1.1 GB) are far larger than the 126 MB L2, so no flush is
 needed between steps.  Synthetic seeded weights stand in for checkpoints.
+
+On one GPU the line also carries, each as its own record:
+  "gemv_sweep"  config 2: GB/s of the batch-1 Q4_0 GEMV on the six sweep
+                shapes, back-to-back launches in one CUDA graph over weight
+                copies that together exceed the L2 (every launch streams from HBM);
+  "configs"     config 1 (1B shape, 32-token prompt + 128 greedy steps) and
+                config 5 (70B shape, KV 2048, 128 greedy steps) on this GPU;
+  "prefill"     config 4 (8B shape, Q8_0 linears), a 512-token prompt through
+                the tensor-core prefill path, then 64 decode steps.
 With N > 1 (torchrun, one rank per GPU) the model is tensor parallel over the N
 GPUs: one sequence, the same total work (strong scaling); the roofline's peak
 is then the N GPUs' aggregate HBM bandwidth.
+
+Roofline.  "frac" is the dominant kernel family's (the Q4 GEMVs, ~3/4 of the
+step): their algorithmic bytes per step / their summed in-graph durations,
+taken from the device timeline of graph-launched steps (each kernel's share =
+last-CTA end minus the previous kernel's last-CTA end, so the shares add up to
+the step).  "step_frac" is the north-star figure: weight + KV bytes per token
+/ the step time / the aggregate HBM bandwidth.
 """
 import argparse
 import json
 import os
+import platform
 import statistics
 import subprocess
 import sys
@@ -35,26 +47,28 @@ WORKLOADS = {
     "8b": dict(cfg=dict(n_layers=32, hidden=4096, n_heads=32, n_kv_heads=8, head_dim=128, ffn=14336,
                         vocab=128256, max_seq=4608, rms_eps=1e-5, rope_theta=500000.0, weight_format=0,
                         tied_embeddings=0),
-               kv=4096, name="llama3-8b-shaped Q4_0 decode, KV pre-filled to 4096 (config 3)"),
+               kv=4096, steps=256, name="llama3-8b-shaped Q4_0 decode, KV pre-filled to 4096 (config 3)"),
     "1b": dict(cfg=dict(n_layers=16, hidden=2048, n_heads=32, n_kv_heads=8, head_dim=64, ffn=8192,
                         vocab=128256, max_seq=256, rms_eps=1e-5, rope_theta=500000.0, weight_format=0,
                         tied_embeddings=1),
-               kv=32, name="llama3.2-1b-shaped Q4_0 decode after a 32-token prompt (config 1)"),
+               kv=32, steps=128, name="llama3.2-1b-shaped Q4_0 decode after a 32-token prompt (config 1)"),
     "70b": dict(cfg=dict(n_layers=80, hidden=8192, n_heads=64, n_kv_heads=8, head_dim=128, ffn=28672,
-                         vocab=128256, max_seq=2176, rms_eps=1e-5, rope_theta=500000.0, weight_format=0,
+                         vocab=128256, max_seq=2304, rms_eps=1e-5, rope_theta=500000.0, weight_format=0,
                          tied_embeddings=0),
-                kv=2048, name="llama3-70b-shaped Q4_0 decode, KV pre-filled to 2048 (config 5)"),
+                kv=2048, steps=128, name="llama3-70b-shaped Q4_0 decode, KV pre-filled to 2048 (config 5)"),
 }
 SEED = 0x5EED
 
-# config 4: the 8B shape with Q8_0 linears, prefill of a 512-token prompt
+# config 4: the 8B shape with Q8_0 linears, prefill of a 512-token prompt + 64 decode steps
 PREFILL = dict(cfg=dict(n_layers=32, hidden=4096, n_heads=32, n_kv_heads=8, head_dim=128, ffn=14336, vocab=128256,
-                        max_seq=576, rms_eps=1e-5, rope_theta=500000.0, weight_format=1, tied_embeddings=0),
-               n=512, name="llama3-8b-shaped Q8_0 prefill of a 512-token prompt (config 4)")
+                        max_seq=640, rms_eps=1e-5, rope_theta=500000.0, weight_format=1, tied_embeddings=0),
+               n=512, decode=64, name="llama3-8b-shaped Q8_0 prefill of a 512-token prompt + 64 decode steps (config 4)")
+
+# config 2: the GEMV sweep (out x in)
+SWEEP = [(2048, 2048), (8192, 2048), (2048, 8192), (14336, 4096), (4096, 14336), (128256, 4096)]
 
 # DRAM bytes per launch of each decode-step GEMV of the 8B shape, from one ncu
-# capture (dram__bytes_read.sum + dram__bytes_write.sum; profiles/
-# decode_step_8b_kv4096_launches.md has the command and the table).
+# capture of a 2-layer model (dram__bytes_read.sum + dram__bytes_write.sum).
 MEASURED_GEMV_DRAM_8B = {"qkv_gemv": 14.27e6, "o_gemv": 9.54e6, "gate_up_gemv": 66.18e6, "down_gemv": 33.18e6,
                          "lm_head_gemv": 296.07e6}
 
@@ -64,8 +78,8 @@ def load_peaks():
     if os.path.exists(p):
         with open(p) as f:
             d = json.load(f)
-        return float(d.get("hbm_gbs", 6650.0)), "measured"
-    return 6650.0, "fallback"
+        return float(d.get("hbm_gbs", 6650.0)), "measured (MEASURED_PEAKS.json hbm_gbs)"
+    return 6650.0, "fallback (6.65 TB/s)"
 
 
 def load_pkg():
@@ -81,24 +95,37 @@ def load_pkg():
     return mod
 
 
+def cpu_model():
+    try:
+        with open("/proc/cpuinfo") as f:
+            for ln in f:
+                if ln.startswith("model name"):
+                    return ln.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return platform.processor() or "unknown"
+
+
 # ----------------------------------------------------------- byte accounting
-def linear_shapes(c):
-    """(N, K) of every quantised linear read per decode token (native GQA)."""
-    D, H, F = c["head_dim"], c["hidden"], c["ffn"]
-    qkv = ((c["n_heads"] + 2 * c["n_kv_heads"]) * D, H)
-    per_layer = [qkv, (H, c["n_heads"] * D), (2 * F, H), (H, F)]
-    return per_layer * c["n_layers"] + [(c["vocab"], H)]
+def linear_shapes(c, tp=1):
+    """(N, K) of every quantised linear read per decode token by one rank (native GQA)."""
+    D, H, F = c["head_dim"], c["hidden"], c["ffn"] // tp
+    hq, hkv = c["n_heads"] // tp, c["n_kv_heads"] // tp
+    qkv = ((hq + 2 * hkv) * D, H)
+    per_layer = [qkv, (H, hq * D), (2 * F, H), (H, F)]
+    return per_layer * c["n_layers"] + [(c["vocab"] // tp, H)]
 
 
 def q_bytes(n, k, c):
-    # Q4: nibbles + fp16 scale = 18 B per 32 weights (Q8_0: 34 B); the tied 1B head has f32 scales (20 B)
+    # Q4: nibbles + fp16 scale = 18 B per 32 weights (Q8_0: 34 B)
     if c["weight_format"] == 1:
         return n * k * 34 // 32
     return n * k * 18 // 32
 
 
-def algo_bytes_per_token(c, S):
-    w = sum(q_bytes(n, k, c) for n, k in linear_shapes(c))
+def algo_bytes_per_token(c, S, tp=1):
+    """Weight + KV (+ norms, embedding row) bytes of one decode token over all ranks."""
+    w = sum(q_bytes(n, k, c) for n, k in linear_shapes(c, tp)) * tp
     if c["tied_embeddings"]:
         w += c["vocab"] * c["hidden"] // 16  # f32 instead of f16 scales on the tied head
     kv = 2 * c["n_layers"] * c["n_kv_heads"] * c["head_dim"] * S * 4
@@ -107,9 +134,11 @@ def algo_bytes_per_token(c, S):
     return w + kv + norms + emb, w, kv
 
 
-def gemv_bytes(kind, c):
-    D, H, F, V = c["head_dim"], c["hidden"], c["ffn"], c["vocab"]
-    n, k = {"qkv_gemv": ((c["n_heads"] + 2 * c["n_kv_heads"]) * D, H), "o_gemv": (H, c["n_heads"] * D),
+def gemv_bytes(kind, c, tp=1):
+    """Algorithmic bytes of one launch of a decode-step GEMV on one rank."""
+    D, H, F, V = c["head_dim"], c["hidden"], c["ffn"] // tp, c["vocab"] // tp
+    hq, hkv = c["n_heads"] // tp, c["n_kv_heads"] // tp
+    n, k = {"qkv_gemv": ((hq + 2 * hkv) * D, H), "o_gemv": (H, hq * D),
             "gate_up_gemv": (2 * F, H), "down_gemv": (H, F), "lm_head_gemv": (V, H)}[kind]
     b = q_bytes(n, k, c) + k * 4 + n * 4
     if kind == "lm_head_gemv" and c["tied_embeddings"]:
@@ -131,60 +160,117 @@ def prefill_prompt(c, n):
 
 
 # ----------------------------------------------------------------- clocks
+_REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+            0x80: "hw_power_brake_slowdown"}
+
+
 class ClockSampler:
-    def __init__(self, device):
-        self.device = device
-        self.proc = None
-        self.lines = []
+    """SM clock and clock-event reasons of this process's GPU, sampled every
+    ~1 ms through NVML (the source nvidia-smi reads) while the timed region
+    runs; falls back to `nvidia-smi -lms 50` without NVML."""
+
+    def __init__(self, cuda_device):
+        self.cuda_device = cuda_device
+        self.sm, self.reasons, self.power = [], set(), []
+        self.max_mhz = None
+        self.source = None
+        self._stop = threading.Event()
+        self._t = None
+        self._proc = None
+        self._lines = []
+
+    def _nvml_handle(self):
+        import pynvml
+        pynvml.nvmlInit()
+        try:  # NVML numbers GPUs without CUDA_VISIBLE_DEVICES: go by PCI bus id
+            import torch
+            pr = torch.cuda.get_device_properties(self.cuda_device)
+            bus = "%08x:%02x:%02x.0" % (pr.pci_domain_id, pr.pci_bus_id, pr.pci_device_id)
+            return pynvml, pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:
+            return pynvml, pynvml.nvmlDeviceGetHandleByIndex(self.cuda_device)
 
     def __enter__(self):
+        try:
+            nv, h = self._nvml_handle()
+            self.max_mhz = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+            get_r = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                nv.nvmlDeviceGetCurrentClocksThrottleReasons
+
+            def run():
+                while not self._stop.is_set():
+                    try:
+                        self.sm.append(float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)))
+                        r = int(get_r(h))
+                        for bit, name in _REASONS.items():
+                            if r & bit:
+                                self.reasons.add(name)
+                    except Exception:
+                        pass
+                    time.sleep(0.001)
+
+            self._t = threading.Thread(target=run, daemon=True)
+            self._t.start()
+            self.source = "nvml, ~1 ms"
+            t_end = time.time() + 2.0
+            while not self.sm and time.time() < t_end:
+                time.sleep(0.001)
+            self.sm.clear()
+            self.reasons.clear()
+        except Exception:
+            self._smi_start()
+        return self
+
+    def _smi_start(self):
         q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.device), "--query-gpu=" + q,
-                                          "--format=csv,noheader,nounits", "-lms", "50"],
-                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
-            self.t.start()
-            # start timing only once the sampler is producing (startup takes ~0.1-1 s)
-            t_end = time.time() + 5.0
-            while not self.lines and time.time() < t_end:
-                time.sleep(0.01)
-            self.lines.clear()
-        except Exception:
-            self.proc = None
-        return self
+            self._proc = subprocess.Popen(["nvidia-smi", "-i", str(self.cuda_device), "--query-gpu=" + q,
+                                           "--format=csv,noheader,nounits", "-lms", "50"],
+                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            def read():
+                for line in self._proc.stdout:
+                    self._lines.append(line.strip())
+
+            self._t = threading.Thread(target=read, daemon=True)
+            self._t.start()
+            t_end = time.time() + 5.0
+            while not self._lines and time.time() < t_end:
+                time.sleep(0.01)
+            self._lines.clear()
+            self.source = "nvidia-smi -lms 50"
+        except Exception:
+            self._proc = None
 
     def __exit__(self, *a):
-        if self.proc:
-            self.proc.terminate()
+        self._stop.set()
+        if self._proc:
+            self._proc.terminate()
             try:
-                self.proc.wait(timeout=5)
+                self._proc.wait(timeout=5)
             except Exception:
-                self.proc.kill()
+                self._proc.kill()
+            names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+            for ln in self._lines:
+                f = [x.strip() for x in ln.split(",")]
+                if len(f) < 9:
+                    continue
+                try:
+                    self.sm.append(float(f[1]))
+                    self.max_mhz = float(f[2])
+                except ValueError:
+                    continue
+                for name, v in zip(names, f[5:9]):
+                    if v.lower() == "active":
+                        self.reasons.add(name)
+        elif self._t:
+            self._t.join(timeout=1.0)
 
     def summary(self):
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
-            f = [x.strip() for x in ln.split(",")]
-            if len(f) < 9:
-                continue
-            try:
-                sm.append(float(f[1]))
-                mx = float(f[2])
-            except ValueError:
-                continue
-            for name, v in zip(names, f[5:9]):
-                if v.lower() == "active":
-                    reasons.add(name)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+        return {"sm_mhz": statistics.median(self.sm) if self.sm else None, "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.sm), "source": self.source}
 
 
 # ------------------------------------------------------------- CPU baseline
@@ -249,6 +335,129 @@ def int8_peak_tops():
     return 2.0 * n ** 3 / (e0.elapsed_time(e1) / 10 / 1000.0) / 1e12
 
 
+# ------------------------------------------------------------ in-graph shares
+def in_graph_ms(m, tok, pos, reps=3):
+    """Per kernel kind: summed in-graph duration (ms) per step and launches per
+    step, from the device timeline of `reps` traced, graph-launched steps."""
+    acc, counts = {}, {}
+    for r in range(reps):
+        tr = m.trace_decode(tok, pos + r)
+        prev = tr[0][1]
+        per = {}
+        for (kind, start, go, ready, end) in tr:
+            per[kind] = per.get(kind, 0) + (end - prev)
+            prev = end
+            if r == 0:
+                counts[kind] = counts.get(kind, 0) + 1
+        for k, v in per.items():
+            acc.setdefault(k, []).append(v / 1e6)
+    return {k: statistics.median(v) for k, v in acc.items()}, counts
+
+
+def decode_record(L, ctx, wl, c, rank, world, K, W, clock_device, with_trace=True, prompt=False):
+    """Time K graph-launched decode steps of workload `wl` (after W warm-up
+    steps), plus the in-graph kernel shares and the roofline fractions.  The
+    KV cache holds wl["kv"] positions: pre-filled with N(0,1) rows, or (prompt)
+    written by a prefill of a wl["kv"]-token prompt."""
+    m = L.Model(ctx, dict(c, tp_rank=rank, tp_size=world))
+    m.init_synthetic(SEED)
+    if world > 1:
+        L.connect_tensor_parallel(m)
+    kv0 = wl["kv"]
+    if prompt:
+        tok0, _ = m.prefill(prefill_prompt(c, kv0), 0, want_logits=False)
+    else:
+        m.kv_fill_synthetic(SEED, kv0)
+        tok0 = 1234 % c["vocab"]
+    assert kv0 + max(K, W) + 8 <= c["max_seq"], "steps exceed the KV capacity"
+    m.time_decode(tok0, kv0, W)  # warm-up (also captures the step graph)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    with ClockSampler(clock_device) as clk:
+        ms = m.time_decode(tok0, kv0, K)
+    if dist is not None:
+        import torch
+        t = torch.tensor([ms], dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    rec = {"m": m, "ms": ms, "kv0": kv0, "tok0": tok0, "clocks": clk.summary()}
+    if with_trace:
+        kind_ms, counts = in_graph_ms(m, tok0, kv0)
+        if world > 1:
+            import torch
+            names = sorted(kind_ms)
+            t = torch.tensor([kind_ms[k] for k in names], dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            kind_ms = {k: float(v) for k, v in zip(names, t.tolist())}
+        rec["kind_ms"], rec["counts"] = kind_ms, counts
+    return rec
+
+
+def roofline(c, wl, rec, K, world, peak_gbs, peak_src, traffic=None):
+    ms_per_step = rec["ms"] / K
+    S_mid = rec["kv0"] + K // 2
+    tot_bytes, w_bytes, kv_bytes = algo_bytes_per_token(c, S_mid, world)
+    step_gbs = tot_bytes / (ms_per_step / 1000.0) / 1e9
+    peak = peak_gbs * world
+    out = {"bound": "hbm", "unit": "GB/s", "peak": round(peak, 1), "peak_source": peak_src,
+           "step_algorithmic_bytes": tot_bytes, "step_achieved_gbs": round(step_gbs, 1),
+           "step_frac": round(step_gbs / peak, 4),
+           "step_frac_definition": "weight + KV (+ norms, embedding row) bytes per token / ms_per_step / "
+                                   "aggregate HBM bandwidth of the n_gpus"}
+    if "kind_ms" in rec:
+        kind_ms, counts = rec["kind_ms"], rec["counts"]
+        gemv = [k for k in kind_ms if k.endswith("_gemv")]
+        g_bytes = sum(gemv_bytes(k, c, world) * counts[k] for k in gemv) * world
+        g_ms = sum(kind_ms[k] for k in gemv)
+        launches = sum(counts[k] for k in gemv)
+        achieved = g_bytes / (g_ms / 1000.0) / 1e9
+        att_bytes = 2 * c["n_layers"] * c["n_kv_heads"] * c["head_dim"] * (rec["kv0"] + 1) * 4
+        out.update({
+            "kernel": "gemv_tma_kernel (every Q4 GEMV of a decode step)",
+            "achieved": round(achieved, 1), "frac": round(achieved / peak, 4),
+            "frac_definition": "GEMV algorithmic bytes per step / the GEMVs' summed in-graph durations "
+                               "(device timeline of graph-launched steps) / aggregate HBM bandwidth",
+            "traffic": traffic, "traffic_unit": "DRAM bytes per GEMV launch (ncu)",
+            "algorithmic_bytes_per_launch": round(g_bytes / world / launches),
+            "gemv_launches_per_step": launches, "gemv_bytes_per_step": g_bytes,
+            "in_graph_ms_per_step": {k: round(v, 4) for k, v in sorted(kind_ms.items())},
+            "in_graph_sum_ms": round(sum(kind_ms.values()), 4),
+            "attention_achieved_gbs": round(att_bytes / (kind_ms["attention"] / 1000.0) / 1e9, 1)
+            if "attention" in kind_ms else None,
+        })
+    return out
+
+
+def run_gemv_sweep(L, ctx, reps=20):
+    """Config 2: device us per launch and GB/s of the Q4_0 x Q8_0 GEMV, every
+    launch streaming its own weight copy from HBM (copies >= 2x the L2)."""
+    import torch
+    dev = torch.device("cuda", ctx.device)
+    peak, _ = load_peaks()
+    out = {}
+    for n, k in SWEEP:
+        wb = n * k // 2 + n * (k // 32) * 2
+        copies = max(2, min(256, -(-(256 << 20) // wb)))
+        codes = [torch.randint(0, 256, (n * k // 2,), dtype=torch.uint8, device=dev) for _ in range(copies)]
+        scl = [(torch.rand(n * (k // 32), device=dev) * 0.004 + 1e-4).half() for _ in range(copies)]
+        x = torch.randn(k, device=dev)
+        y = torch.empty(n, device=dev)
+        us = L.time_gemv(ctx, [t.data_ptr() for t in codes], [t.data_ptr() for t in scl], x.data_ptr(),
+                         y.data_ptr(), n, k, reps)
+        by = n * k * 18 // 32 + 4 * k + 4 * n
+        out["%dx%d" % (n, k)] = {"us_per_launch": round(us, 3), "algorithmic_bytes": by,
+                                 "gbs": round(by / (us * 1e-6) / 1e9, 1), "frac": round(by / (us * 1e-6) / 1e9 / peak, 4),
+                                 "weight_copies": copies}
+        del codes, scl
+        torch.cuda.empty_cache()
+    return {"metric": "batch-1 Q4_0 GEMV effective GB/s (config 2)",
+            "method": "llmrs_time_gemv: back-to-back launches in one CUDA graph with programmatic overlap, each "
+                      "on its own weight copy (copies together >= 256 MB > L2), %d graph replays" % reps,
+            "peak_gbs": peak, "shapes": out}
+
+
 def run_prefill(L, ctx, args):
     c = dict(PREFILL["cfg"])
     if args.layers:
@@ -258,13 +467,16 @@ def run_prefill(L, ctx, args):
     m.init_synthetic(SEED)
     ids = prefill_prompt(c, n)
     m.time_prefill(ids, 0, args.warmup)  # warm-up
-    with ClockSampler(int(os.environ.get("LOCAL_RANK", "0"))) as clk:
+    with ClockSampler(ctx.device) as clk:
         ms = m.time_prefill(ids, 0, max(1, min(args.steps, 10)))
     e2e = []
     for _ in range(3):
         t0 = time.perf_counter()
         m.prefill(ids, 0, want_logits=True)
         e2e.append(time.perf_counter() - t0)
+    # the 64 decode steps that follow the prompt (config 4), device-timed
+    tok, _ = m.prefill(ids, 0, want_logits=False)
+    dms = m.time_decode(tok, n, PREFILL["decode"])
     m.close()
     lin, att = prefill_ops(c, n)
     try:
@@ -277,6 +489,7 @@ def run_prefill(L, ctx, args):
            "dtype": "q8_0 x q8_0 (exact integer block dots on tcgen05 with bf16 operands, f32 block sums)",
            "e2e": {"value": round(n / statistics.median(e2e), 1), "unit": "tokens/s",
                    "h2d_bytes_per_step": 4 * n, "d2h_bytes_per_step": 4 * c["vocab"] + 8},
+           "decode_after_prompt": {"steps": PREFILL["decode"], "tokens_per_s": round(PREFILL["decode"] / (dms / 1000.0), 1)},
            "ops_per_prefill": {"linear_int_ops": lin, "attention_f32_flops": att},
            "achieved_tops": round(tops, 1), "clocks": clk.summary()}
     if peak:
@@ -288,8 +501,24 @@ def run_prefill(L, ctx, args):
     if not args.no_cpu:
         v, cores, t = cpu_prefill_baseline()
         out["cpu_baseline"] = {"value": round(v, 3), "unit": "tokens/s", "cores": cores, "kind": "port",
+                               "cpu": cpu_model(),
                                "sample": "32-token prompt through 2 of the 32 layers (%.1f s scaled to 32 layers)" % t}
     return out
+
+
+def run_config(L, ctx, name, peak, peak_src, args):
+    """One N=1 sub-record: decode tokens/s of another config on this GPU."""
+    wl = WORKLOADS[name]
+    c = dict(wl["cfg"])
+    K = wl["steps"]
+    rec = decode_record(L, ctx, wl, c, 0, 1, K, max(3, args.warmup), ctx.device, prompt=name == "1b")
+    m = rec["m"]
+    toks = m.generate(rec["tok0"], rec["kv0"], 8)  # the greedy loop on the device
+    m.close()
+    return {"metric": "batch-1 greedy decode tokens/s", "workload": wl["name"], "value": round(K / (rec["ms"] / 1000.0), 2),
+            "unit": "tokens/s", "steps": K, "ms_per_step": round(rec["ms"] / K, 4),
+            "roofline": roofline(c, wl, rec, K, 1, peak, peak_src), "clocks": rec["clocks"],
+            "greedy_tokens_sample": [int(t) for t in toks]}
 
 
 # ------------------------------------------------------------------ our arm
@@ -301,65 +530,21 @@ def run_ours(args, rank, world):
     if args.layers:
         c["n_layers"] = args.layers
     ctx = L.Context(local)
-    # N > 1: tensor parallel over the N GPUs (one sequence, strong scaling)
-    m = L.Model(ctx, dict(c, tp_rank=rank, tp_size=world))
-    m.init_synthetic(SEED)
-    m.kv_fill_synthetic(SEED, wl["kv"])
-    if world > 1:
-        L.connect_tensor_parallel(m)
-    kv0 = wl["kv"]
-    tok0 = 1234 % c["vocab"]
     K, W = args.steps, args.warmup
-    assert kv0 + max(K, W) + 1 <= c["max_seq"], "steps exceed the KV capacity"
-    # warm-up (also captures the step graph)
-    m.time_decode(tok0, kv0, W)
-    dist = None
-    if world > 1:
-        import torch.distributed as dist
-        dist.barrier()
-    with ClockSampler(local) as clk:
-        ms = m.time_decode(tok0, kv0, K)
-    if dist is not None:
-        import torch
-        t = torch.tensor([ms], dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+    rec = decode_record(L, ctx, wl, c, rank, world, K, W, local)
+    m = rec["m"]
+    ms = rec["ms"]
     ms_per_step = ms / K
     value = K / (ms / 1000.0)  # one sequence decoded by all ranks together
-    # per-kernel durations (kernel by kernel, events around each launch)
-    prof = [m.profile_decode(tok0, kv0 + i) for i in range(3)]
-    per_kind = {}
-    for run in prof:
-        agg = {}
-        for kind, t in run:
-            agg.setdefault(kind, []).append(t)
-        for kind, ts in agg.items():
-            per_kind.setdefault(kind, []).append(sum(ts))
-    kind_ms = {k: statistics.median(v) for k, v in per_kind.items()}
-    kind_count = {}
-    for kind, _ in prof[0]:
-        kind_count[kind] = kind_count.get(kind, 0) + 1
-    if world > 1:  # the slowest rank sets the pace
-        import torch
-        import torch.distributed as dist
-        names = sorted(kind_ms)
-        t = torch.tensor([kind_ms[k] for k in names], dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        kind_ms = {k: float(v) for k, v in zip(names, t.tolist())}
-    gemv_kinds = [k for k in kind_ms if k.endswith("_gemv")]
-    gemv_bytes_step = sum(gemv_bytes(k, c) * kind_count[k] for k in gemv_kinds)
-    gemv_ms_step = sum(kind_ms[k] for k in gemv_kinds)
-    gemv_launches = sum(kind_count[k] for k in gemv_kinds)
     traffic = None
     if args.workload == "8b" and not args.layers and world == 1:
-        traffic = round(sum(MEASURED_GEMV_DRAM_8B[k] * kind_count[k] for k in gemv_kinds) / gemv_launches)
+        counts = rec["counts"]
+        gk = [k for k in counts if k.endswith("_gemv")]
+        traffic = round(sum(MEASURED_GEMV_DRAM_8B[k] * counts[k] for k in gk) / sum(counts[k] for k in gk))
     peak, peak_src = load_peaks()
-    peak *= world  # aggregate HBM bandwidth of the N GPUs
-    achieved = gemv_bytes_step / (gemv_ms_step / 1000.0) / 1e9
-    S_mid = kv0 + K // 2
-    tot_bytes, w_bytes, kv_bytes = algo_bytes_per_token(c, S_mid)
-    step_gbs = tot_bytes / (ms_per_step / 1000.0) / 1e9
+    roof = roofline(c, wl, rec, K, world, peak, peak_src, traffic)
     # end to end through the C ABI: token in from host memory, argmax (+err word) back
+    kv0, tok0 = rec["kv0"], rec["tok0"]
     E = min(K, 64)
     m.decode_step(tok0, kv0, want_logits=False)
     t0 = time.perf_counter()
@@ -367,12 +552,23 @@ def run_ours(args, rank, world):
     for i in range(E):
         tok, _ = m.decode_step(tok, kv0 + i, want_logits=False)
     e2e_s = time.perf_counter() - t0
+    ranks = [{"rank": rank, "local_rank": local, "device": local}]
     if world > 1:
         import torch
         import torch.distributed as dist
         t = torch.tensor([e2e_s], dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_s = float(t.item())
+        try:
+            name = torch.cuda.get_device_properties(local).name
+            pr = torch.cuda.get_device_properties(local)
+            bus = "%04x:%02x:%02x" % (pr.pci_domain_id, pr.pci_bus_id, pr.pci_device_id)
+        except Exception:
+            name, bus = None, None
+        mine = {"rank": rank, "local_rank": local, "device": local, "gpu": name, "pci": bus,
+                "tp_connected": True, "host": platform.node()}
+        ranks = [None] * world
+        dist.all_gather_object(ranks, mine)
     e2e_val = E / e2e_s
     kernels_step = m.decode_kernel_count()
     out = {
@@ -389,35 +585,31 @@ def run_ours(args, rank, world):
         "vs_baseline": None,
         "dtype": "q4_0 x q8_0 (int8 dot, f32 accumulate), f32 KV",
         "data": "synthetic (seeded random-init weights of the named shape; KV pre-filled N(0,1))",
-        "config": {"workload": wl["name"], "model": args.workload, "global_batch": 1, "seq_len": S_mid,
-                   "kv_prefill": kv0, "parallelism": "tp%d" % world,
-                   "l2": "inputs larger than L2 (weights %.2f GB + KV %.2f GB per token)" % (w_bytes / 1e9,
-                                                                                              kv_bytes / 1e9)},
-        "roofline": {"bound": "hbm", "kernel": "gemv_tma_kernel (all Q4 GEMVs of one decode step)",
-                     "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                     "frac": round(achieved / peak, 4), "traffic": traffic, "traffic_unit": "bytes per launch",
-                     "algorithmic_bytes_per_launch": round(gemv_bytes_step / gemv_launches), "peak_source": peak_src,
-                     "gemv_launches_per_step": gemv_launches, "gemv_bytes_per_step": gemv_bytes_step,
-                     "per_kernel_ms": {k: round(v, 4) for k, v in kind_ms.items()},
-                     "step_algorithmic_bytes": tot_bytes, "step_achieved_gbs": round(step_gbs, 1),
-                     "step_frac": round(step_gbs / peak, 4)},
+        "config": {"workload": wl["name"], "model": args.workload, "global_batch": 1,
+                   "seq_len": kv0 + K // 2, "kv_prefill": kv0, "parallelism": "tp%d" % world,
+                   "l2": "inputs larger than L2, no flush (%.2f GB read per token)" % (roof["step_algorithmic_bytes"] / 1e9)},
+        "roofline": roof,
         "e2e": {"value": round(e2e_val, 2), "unit": "tokens/s", "h2d_bytes_per_step": 8,
-                "d2h_bytes_per_step": 8},
+                "d2h_bytes_per_step": 8, "api": "llmrs_decode_step (token in, argmax + error word out)"},
         "gpu_launches": world * kernels_step * K,
-        "clocks": clk.summary(),
+        "kernels_per_step_per_rank": kernels_step,
+        "ranks": ranks,
+        "clocks": rec["clocks"],
     }
-    if world == 1 and args.workload == "8b" and not args.layers and not args.no_prefill:
-        m.close()
-        out["prefill"] = run_prefill(L, ctx, args)
-        m = None
+    m.close()
+    if world == 1 and not args.layers and not args.no_extra and args.workload == "8b":
+        out["gemv_sweep"] = run_gemv_sweep(L, ctx)
+        out["configs"] = {"config1_1b": run_config(L, ctx, "1b", peak, peak_src, args),
+                          "config5_70b": run_config(L, ctx, "70b", peak, peak_src, args)}
+        if not args.no_prefill:
+            out["prefill"] = run_prefill(L, ctx, args)
     if rank == 0 and world == 1 and not args.no_cpu:
-        n_cpu = 2 if args.workload != "70b" else 1
+        n_cpu = 24 if args.workload != "70b" else 2
         v, cores, times = cpu_baseline(wl, n_cpu)
         out["cpu_baseline"] = {"value": round(v, 3), "unit": "tokens/s", "cores": cores, "kind": "port",
-                               "sample": "%d decode tokens of the same model at KV %d (median of %s s)" %
-                                         (n_cpu, kv0 + 1, [round(t, 2) for t in times])}
-    if m is not None:
-        m.close()
+                               "cpu": cpu_model(),
+                               "sample": "%d decode tokens of the same model at KV %d.. (median of %.1f s of work)" %
+                                         (n_cpu, kv0 + 1, sum(times))}
     ctx.close()
     return out
 
@@ -428,14 +620,17 @@ def prefill_reference(args):
     v, cores, t = cpu_prefill_baseline()
     return {"metric": "prefill tokens/s", "value": round(v, 3), "unit": "tokens/s", "workload": PREFILL["name"],
             "cpu_baseline": {"value": round(v, 3), "unit": "tokens/s", "cores": cores, "kind": "port",
+                             "cpu": cpu_model(),
                              "sample": "32-token prompt through 2 of the 32 layers (%.1f s scaled to 32 layers)" % t}}
 
 
 def run_reference(args, rank, world):
+    """The reference's CPU path (restated in C, oracle/) on the host cores:
+    the Rust reference cannot be built here (no Rust toolchain)."""
     if rank != 0:
         return None
     wl = WORKLOADS[args.workload]
-    n = max(1, min(args.steps, 4 if args.workload != "70b" else 2))
+    n = max(1, min(args.steps, 32 if args.workload != "70b" else 2))
     v, cores, times = cpu_baseline(wl, n)
     return {
         "impl": "reference",
@@ -447,9 +642,9 @@ def run_reference(args, rank, world):
         "data": "synthetic (seeded random-init weights; KV pre-filled N(0,1))",
         "config": {"workload": wl["name"], "model": args.workload, "kv_prefill": wl["kv"],
                    "parallelism": "cpu (rayon-equivalent OpenMP over 512-row chunks)"},
-        "cpu_baseline": {"value": round(v, 3), "unit": "tokens/s", "cores": cores, "kind": "port",
-                         "sample": "%d decode tokens at KV %d; reference CPU path restated in C (oracle/), "
-                                   "Rust reference not buildable here" % (n, wl["kv"] + 1)},
+        "cpu_baseline": {"value": round(v, 3), "unit": "tokens/s", "cores": cores, "kind": "port", "cpu": cpu_model(),
+                         "sample": "%d decode tokens at KV %d..; reference CPU path restated in C (oracle/), "
+                                   "Rust reference not buildable here (%.1f s of work)" % (n, wl["kv"] + 1, sum(times))},
         "e2e": {"value": round(v, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "prefill": prefill_reference(args),
     }
@@ -463,7 +658,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="8b")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
-    ap.add_argument("--no-prefill", action="store_true", help="skip the config-4 prefill leg")
+    ap.add_argument("--no-prefill", action="store_true", help="skip the config-4 prefill record")
+    ap.add_argument("--no-extra", action="store_true", help="skip the sweep, config-1/5 and prefill records")
     ap.add_argument("--prefill-only", action="store_true",
                     help="run only the config-4 prefill leg (with --layers: a small case for ncu; not a bench line)")
     ap.add_argument("--layers", type=int, default=0,

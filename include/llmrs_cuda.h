@@ -269,6 +269,17 @@ int llmrs_model_profile_decode(llmrs_model *model, int token, int pos, float *ms
  * end (globaltimer ns); kinds[i] as in profile_decode.
  * *n: in = capacity (kernels), out = kernels of the step */
 int llmrs_model_trace_decode(llmrs_model *model, int token, int pos, unsigned long long *h_marks, int *kinds, int *n);
+/* Device time per launch of the batch-1 GEMV of llmrs_matmul_transposed_q4/_q8
+ * (m = 1): the `copies` weight matrices [n][k] (h_codes[i] / h_scales[i]: device
+ * pointers, the layout of llmrs_matmul_transposed_q4) are multiplied with d_x[k]
+ * into d_y[n] back to back as one CUDA graph, each launch overlapping its
+ * predecessor's tail as consecutive GEMVs of a decode step do; the graph is
+ * replayed `reps` times after one warm-up replay.  Copies that together exceed
+ * the L2 make every launch stream its weights from HBM.  A measurement helper
+ * (the reference's bench binary, src/bench/main.rs, times its ops on the host). */
+int llmrs_time_gemv(llmrs_ctx *ctx, int weight_format, int scale_dtype, const void *const *h_codes,
+                    const void *const *h_scales, int copies, const float *d_x, float *d_y, int n, int k, int reps,
+                    float *us_per_launch);
 /* time `iters` device-resident decode steps (graph replays) with CUDA events
  * on the model's stream; *ms_total = elapsed ms; the KV position advances */
 int llmrs_model_time_decode(llmrs_model *model, int token, int pos, int iters, float *ms_total);

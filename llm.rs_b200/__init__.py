@@ -28,7 +28,7 @@ WFMT_Q4_0, WFMT_Q8_0 = 0, 1
 (W_Q, W_K, W_V, W_O, W_GATE_UP, W_DOWN, W_ATTN_NORM, W_MLP_NORM, W_EMBED, W_FINAL_NORM,
  W_LM_HEAD) = range(11)
 
-# every symbol include/llmrs_cuda.h declares (checked by tests/test_capi.py)
+# every symbol include/llmrs_cuda.h declares (checked by tests/test_synth_and_capi.py)
 EXPORTS = [
     "llmrs_last_error", "llmrs_version", "llmrs_device_count", "llmrs_ctx_create", "llmrs_ctx_destroy",
     "llmrs_ctx_set_stream", "llmrs_malloc", "llmrs_free", "llmrs_h2d", "llmrs_d2h", "llmrs_d2d",
@@ -40,7 +40,7 @@ EXPORTS = [
     "llmrs_model_set_weight", "llmrs_kv_fill", "llmrs_kv_fill_synthetic", "llmrs_kv_read",
     "llmrs_decode_step", "llmrs_generate", "llmrs_prefill", "llmrs_model_logits", "llmrs_rope_table",
     "llmrs_model_decode_kernel_count", "llmrs_model_time_decode", "llmrs_model_time_prefill",
-    "llmrs_model_profile_decode",
+    "llmrs_model_profile_decode", "llmrs_time_gemv",
     "llmrs_attention_decode", "llmrs_attention_decode_noalloc", "llmrs_attention_prefill",
     "llmrs_sample", "llmrs_model_sample", "llmrs_model_trace_decode",
     "llmrs_model_tp_region", "llmrs_model_tp_connect", "llmrs_ipc_get_handle", "llmrs_ipc_open_handle",
@@ -126,6 +126,7 @@ def lib():
         "llmrs_rope_table": (ci, [ci, ci, cf, vp, vp]),
         "llmrs_model_decode_kernel_count": (ci, [vp, ip]),
         "llmrs_model_time_decode": (ci, [vp, ci, ci, ci, fp]),
+        "llmrs_time_gemv": (ci, [vp, ci, ci, vp, vp, ci, vp, vp, ci, ci, ci, fp]),
         "llmrs_model_time_prefill": (ci, [vp, vp, ci, ci, ci, fp]),
         "llmrs_model_profile_decode": (ci, [vp, ci, ci, vp, vp, ip]),
         "llmrs_attention_decode": (ci, [vp, vp, vp, vp, vp, vp, vp, ci, ci, ci, ci, ci]),
@@ -550,6 +551,20 @@ class Model:
         check(lib().llmrs_model_time_prefill(self.h, _ptr(ids), ids.size, int(start_pos), int(iters),
                                              ctypes.byref(ms)))
         return ms.value
+
+
+def time_gemv(ctx, codes, scales, x, y, n, k, reps, fmt=WFMT_Q4_0, scale_dtype=F16):
+    """Device microseconds per launch of the batch-1 GEMV (llmrs_time_gemv):
+    `codes` / `scales` are device addresses (ints) of weight copies [n][k] that
+    are multiplied with x[k] into y[n] back to back in one CUDA graph."""
+    assert len(codes) == len(scales) and codes
+    c = (ctypes.c_void_p * len(codes))(*[int(p) for p in codes])
+    s = (ctypes.c_void_p * len(scales))(*[int(p) for p in scales])
+    us = ctypes.c_float(0)
+    check(lib().llmrs_time_gemv(ctx.h, int(fmt), int(scale_dtype), ctypes.cast(c, ctypes.c_void_p),
+                                ctypes.cast(s, ctypes.c_void_p), len(codes), ctypes.c_void_p(int(x)),
+                                ctypes.c_void_p(int(y)), int(n), int(k), int(reps), ctypes.byref(us)))
+    return us.value
 
 
 def connect_tensor_parallel(model, group=None):

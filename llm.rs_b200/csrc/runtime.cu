@@ -1568,6 +1568,77 @@ int llmrs_model_trace_decode(llmrs_model *m, int token, int pos, unsigned long l
     return check_state_err(m, err);
 }
 
+int llmrs_time_gemv(llmrs_ctx *ctx, int weight_format, int scale_dtype, const void *const *h_codes,
+                    const void *const *h_scales, int copies, const float *d_x, float *d_y, int n, int k, int reps,
+                    float *us_per_launch)
+{
+    LLMRS_CHECK_ARG(ctx && h_codes && h_scales && d_x && d_y && us_per_launch, "NULL argument");
+    LLMRS_CHECK_ARG(copies > 0 && copies <= 4096 && reps > 0 && n > 0 && k > 0, "bad sizes");
+    LLMRS_CHECK_ARG(weight_format == LLMRS_WFMT_Q4_0 || weight_format == LLMRS_WFMT_Q8_0, "bad weight format");
+    LLMRS_CHECK_ARG(scale_dtype == LLMRS_F16 || scale_dtype == LLMRS_F32, "bad scale dtype");
+    cudaSetDevice(ctx->device);
+    std::vector<GemvPlan> plans((size_t)copies);
+    for (int i = 0; i < copies; i++) {
+        LLMRS_CHECK_ARG(h_codes[i] && h_scales[i], "NULL weight copy %d", i);
+        LLMRS_TRY(gemv_plan(&plans[i], h_codes[i], h_scales[i], n, k, weight_format, scale_dtype, false, ctx->sms));
+    }
+    cudaStream_t s = ctx->stream;
+    // one graph: every copy once, back to back, each launch overlapping its predecessor's tail
+    cudaGraph_t g = nullptr;
+    cudaGraphExec_t ge = nullptr;
+    LLMRS_CUDA_TRY(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+    int rc = LLMRS_OK;
+    for (int i = 0; i < copies && rc == LLMRS_OK; i++) {
+        GemvParams p{};
+        p.w = reinterpret_cast<const uint8_t *>(h_codes[i]);
+        p.scales = h_scales[i];
+        p.N = n;
+        p.K = k;
+        p.x = d_x;
+        p.y = d_y;
+        p.err = ctx->d_err;
+        rc = gemv_launch(plans[i], p, PRO_F32, EPI_STORE, s, i > 0);
+    }
+    cudaError_t e = cudaStreamEndCapture(s, &g);
+    if (rc != LLMRS_OK) {
+        if (g)
+            cudaGraphDestroy(g);
+        return rc;
+    }
+    if (e != cudaSuccess)
+        return fail(LLMRS_ECUDA, "gemv timing capture: %s", cudaGetErrorString(e));
+    e = cudaGraphInstantiate(&ge, g, 0);
+    cudaGraphDestroy(g);
+    if (e != cudaSuccess)
+        return fail(LLMRS_ECUDA, "gemv timing graph: %s", cudaGetErrorString(e));
+    cudaEvent_t e0 = nullptr, e1 = nullptr;
+    float ms = 0.0f;
+    e = cudaGraphLaunch(ge, s); // warm-up
+    if (e == cudaSuccess)
+        e = cudaEventCreate(&e0);
+    if (e == cudaSuccess)
+        e = cudaEventCreate(&e1);
+    if (e == cudaSuccess)
+        e = cudaEventRecord(e0, s);
+    for (int r = 0; r < reps && e == cudaSuccess; r++)
+        e = cudaGraphLaunch(ge, s);
+    if (e == cudaSuccess)
+        e = cudaEventRecord(e1, s);
+    if (e == cudaSuccess)
+        e = cudaEventSynchronize(e1);
+    if (e == cudaSuccess)
+        e = cudaEventElapsedTime(&ms, e0, e1);
+    if (e0)
+        cudaEventDestroy(e0);
+    if (e1)
+        cudaEventDestroy(e1);
+    cudaGraphExecDestroy(ge);
+    if (e != cudaSuccess)
+        return fail(LLMRS_ECUDA, "gemv timing: %s", cudaGetErrorString(e));
+    *us_per_launch = ms * 1000.0f / (float)((size_t)reps * copies);
+    return ctx_check_err(ctx);
+}
+
 int llmrs_model_time_decode(llmrs_model *m, int token, int pos, int iters, float *ms_total)
 {
     LLMRS_CHECK_ARG(m && ms_total && iters > 0, "bad arguments");
