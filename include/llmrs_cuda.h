@@ -174,6 +174,14 @@ int llmrs_sample(llmrs_ctx *ctx, const float *d_logits, int vocab, const int *h_
 /* CpuBackend::quantize_row_q8_0 (src/backend/cpu.rs:663-745) for rows of k
  * values: codes [rows][k] and f32 scales [rows][k/32]; bit-exact */
 int llmrs_quantize_row_q8_0(llmrs_ctx *ctx, const float *d_x, int8_t *d_q, float *d_s, int rows, int k);
+/* CpuBackend::rms_norm then quantize_row_q8_0 of one row of k values
+ * (src/backend/cpu.rs:359-393, 724-743) exactly as the decode GEMVs' fused
+ * prologue computes them (its thread count and reduction tree; the sum of
+ * squares is tree-ordered, so a value within rounding of a Q8_0 boundary can
+ * take the neighbouring code): codes [k], f32 scales [k/32].  For parity
+ * checks of that prologue; d_x, d_w and d_q 16-byte aligned, k <= 38912. */
+int llmrs_rms_norm_quantize_q8_0(llmrs_ctx *ctx, const float *d_x, const float *d_w, int8_t *d_q, float *d_s, int k,
+                                 float eps);
 /* Tensor::quantize_q4 (src/core/tensor.rs:102-167): n values -> planar nibbles
  * [(n+1)/2] and f32 scales [(n+31)/32]; bit-exact */
 int llmrs_quantize_q4(llmrs_ctx *ctx, const float *d_w, size_t n, uint8_t *d_qs, float *d_scales);
@@ -290,8 +298,10 @@ int llmrs_model_time_decode(llmrs_model *model, int token, int pos, int iters, f
  * exchange IPC handles of their regions (any host channel), open the others'
  * and connect; decode calls then run on all ranks in the same order with the
  * same token/position, every rank gets the same greedy token, and logits are
- * the rank's vocab shard (vocab/tp floats).  A peer that stops answering
- * makes the waiting kernel give up after ~5 s with LLMRS_EDEVICE. */
+ * the rank's vocab shard (vocab/tp floats).  A peer that stops answering makes
+ * the waiting kernels give up after the peer timeout (5 s unless set) and the
+ * step return LLMRS_ETIMEDOUT; the context stays usable, and the ranks resume
+ * with llmrs_model_tp_resync. */
 #define LLMRS_IPC_HANDLE_BYTES 64
 /* the region of this rank (device pointer and size) */
 int llmrs_model_tp_region(llmrs_model *model, void **d_region, size_t *bytes);
@@ -302,6 +312,20 @@ int llmrs_ipc_get_handle(const void *d_ptr, void *handle_out);
 /* map another process's region on `device` (peer access over NVLink) */
 int llmrs_ipc_open_handle(int device, const void *handle, void **d_ptr_out);
 int llmrs_ipc_close_handle(int device, void *d_ptr);
+/* the longest a decode-step kernel waits for another rank's partial sums or
+ * argmax key before the step fails with LLMRS_ETIMEDOUT (default 5000 ms;
+ * 1 .. 600000); the step graph is rebuilt on its next launch */
+int llmrs_model_set_peer_timeout(llmrs_model *model, int timeout_ms);
+/* decode steps this rank has completed (the count its exchange tags derive
+ * from; ranks that ran the same steps agree) */
+int llmrs_model_tp_epoch(llmrs_model *model, unsigned long long *epoch);
+/* After a step that timed out on some rank (ranks then disagree on the step
+ * count): every rank calls this with the same epoch (e.g. the maximum of
+ * llmrs_model_tp_epoch over the ranks), while no rank has a step running
+ * (a host barrier before and after).  Clears the device error word and sets
+ * this rank's step count and arrival counters so the next step's exchanges
+ * match on every rank.  No counterpart in the reference (one device). */
+int llmrs_model_tp_resync(llmrs_model *model, unsigned long long epoch);
 
 #if defined(__GNUC__)
 #pragma GCC visibility pop

@@ -36,7 +36,7 @@ EXPORTS = [
     "llmrs_matmul_transposed_q4", "llmrs_matmul_transposed_q8", "llmrs_matmul_transposed_f32",
     "llmrs_matmul", "llmrs_matmul_slice", "llmrs_add_assign", "llmrs_silu_mul", "llmrs_rope_inplace",
     "llmrs_rms_norm", "llmrs_softmax", "llmrs_scale", "llmrs_copy_from", "llmrs_quantize_row_q8_0",
-    "llmrs_quantize_q4", "llmrs_model_create", "llmrs_model_destroy", "llmrs_model_init_synthetic",
+    "llmrs_quantize_q4", "llmrs_rms_norm_quantize_q8_0", "llmrs_model_create", "llmrs_model_destroy", "llmrs_model_init_synthetic",
     "llmrs_model_set_weight", "llmrs_kv_fill", "llmrs_kv_fill_synthetic", "llmrs_kv_read",
     "llmrs_decode_step", "llmrs_generate", "llmrs_prefill", "llmrs_model_logits", "llmrs_rope_table",
     "llmrs_model_decode_kernel_count", "llmrs_model_time_decode", "llmrs_model_time_prefill",
@@ -44,7 +44,7 @@ EXPORTS = [
     "llmrs_attention_decode", "llmrs_attention_decode_noalloc", "llmrs_attention_prefill",
     "llmrs_sample", "llmrs_model_sample", "llmrs_model_trace_decode",
     "llmrs_model_tp_region", "llmrs_model_tp_connect", "llmrs_ipc_get_handle", "llmrs_ipc_open_handle",
-    "llmrs_ipc_close_handle",
+    "llmrs_ipc_close_handle", "llmrs_model_set_peer_timeout", "llmrs_model_tp_epoch", "llmrs_model_tp_resync",
 ]
 IPC_HANDLE_BYTES = 64
 
@@ -112,6 +112,7 @@ def lib():
         "llmrs_copy_from": (ci, [vp, vp, vp, sz]),
         "llmrs_quantize_row_q8_0": (ci, [vp, vp, vp, vp, ci, ci]),
         "llmrs_quantize_q4": (ci, [vp, vp, sz, vp, vp]),
+        "llmrs_rms_norm_quantize_q8_0": (ci, [vp, vp, vp, vp, vp, ci, cf]),
         "llmrs_model_create": (ci, [vp, ctypes.POINTER(Config), pp]),
         "llmrs_model_destroy": (ci, [vp]),
         "llmrs_model_init_synthetic": (ci, [vp, ctypes.c_uint64]),
@@ -140,6 +141,9 @@ def lib():
         "llmrs_ipc_get_handle": (ci, [vp, vp]),
         "llmrs_ipc_open_handle": (ci, [ci, vp, pp]),
         "llmrs_ipc_close_handle": (ci, [ci, vp]),
+        "llmrs_model_set_peer_timeout": (ci, [vp, ci]),
+        "llmrs_model_tp_epoch": (ci, [vp, ctypes.POINTER(ctypes.c_uint64)]),
+        "llmrs_model_tp_resync": (ci, [vp, ctypes.c_uint64]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -383,6 +387,14 @@ class CudaBackend:
         check(lib().llmrs_quantize_row_q8_0(self.ctx.h, x.ptr, q.ptr, s.ptr, rows, k))
         return q, s
 
+    def rms_norm_quantize_q8_0(self, x, w, eps):
+        """RMSNorm + Q8_0 of one row as the decode GEMV prologue computes it: (codes, scales)."""
+        k = x.size
+        q = DeviceTensor(self.ctx, (k,), np.int8)
+        s = DeviceTensor(self.ctx, (k // 32,), np.float32)
+        check(lib().llmrs_rms_norm_quantize_q8_0(self.ctx.h, x.ptr, w.ptr, q.ptr, s.ptr, k, eps))
+        return q.numpy(), s.numpy()
+
     def quantize_q4(self, w):
         n = w.size
         qs = DeviceTensor(self.ctx, ((n + 1) // 2,), np.uint8)
@@ -508,6 +520,20 @@ class Model:
             regions[q] = ptr.value
         check(lib().llmrs_model_tp_connect(self.h, regions))
 
+    def set_peer_timeout(self, ms):
+        """Longest wait (ms) of a decode-step kernel for another rank."""
+        check(lib().llmrs_model_set_peer_timeout(self.h, int(ms)))
+
+    def tp_epoch(self):
+        """Decode steps this rank has completed."""
+        e = ctypes.c_uint64(0)
+        check(lib().llmrs_model_tp_epoch(self.h, ctypes.byref(e)))
+        return e.value
+
+    def tp_resync(self, epoch):
+        """Set this rank's step count (and arrival counters) to `epoch`; see resync_tensor_parallel."""
+        check(lib().llmrs_model_tp_resync(self.h, int(epoch)))
+
     def decode_kernel_count(self):
         n = ctypes.c_int(0)
         check(lib().llmrs_model_decode_kernel_count(self.h, ctypes.byref(n)))
@@ -565,6 +591,22 @@ def time_gemv(ctx, codes, scales, x, y, n, k, reps, fmt=WFMT_Q4_0, scale_dtype=F
                                 ctypes.cast(s, ctypes.c_void_p), len(codes), ctypes.c_void_p(int(x)),
                                 ctypes.c_void_p(int(y)), int(n), int(k), int(reps), ctypes.byref(us)))
     return us.value
+
+
+def resync_tensor_parallel(model, group=None):
+    """After a decode step that failed on some rank (LLMRS_ETIMEDOUT): every
+    rank calls this, with no step running.  The ranks agree on the largest
+    completed-step count and set it (llmrs_model_tp_resync) between two
+    barriers, so the next step's exchanges match again.  Returns that count."""
+    import torch.distributed as dist
+
+    dist.barrier(group)
+    epochs = [None] * dist.get_world_size(group)
+    dist.all_gather_object(epochs, int(model.tp_epoch()), group=group)
+    agreed = max(epochs)
+    model.tp_resync(agreed)
+    dist.barrier(group)
+    return agreed
 
 
 def connect_tensor_parallel(model, group=None):

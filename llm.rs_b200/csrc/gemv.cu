@@ -183,6 +183,25 @@ __global__ void __launch_bounds__(SIMPLE_THREADS) gemv_simple_kernel(const GemvP
         argmax_finalize(p, best, threadIdx.x, SIMPLE_THREADS, 1);
 }
 
+// RMSNorm + Q8_0 of one row exactly as the decode GEMVs' prologue computes it
+// (the same PRO_THREADS threads, block mapping and reduction tree), codes in
+// natural order; for parity checks of that prologue.
+__global__ void __launch_bounds__(PRO_THREADS) norm_quant_kernel(const GemvParams p, int8_t *q, float *s)
+{
+    extern __shared__ __align__(16) uint8_t smem[];
+    const int nb = p.K >> 5;
+    uint32_t *act = reinterpret_cast<uint32_t *>(smem);
+    float *act_s = reinterpret_cast<float *>(smem + (size_t)nb * 32);
+    int *act_c = reinterpret_cast<int *>(act_s + nb);
+    float *red = reinterpret_cast<float *>(act_c + nb);
+    load_activation<1, PRO_NORM>(p, act, act_s, act_c, red, threadIdx.x, PRO_THREADS, 1, nullptr);
+    named_bar_sync(1, PRO_THREADS);
+    for (int i = threadIdx.x; i < nb * 8; i += PRO_THREADS)
+        reinterpret_cast<uint32_t *>(q)[i] = act[i];
+    for (int b = threadIdx.x; b < nb; b += PRO_THREADS)
+        s[b] = act_s[b];
+}
+
 constexpr int SIMPLE_SMEM_MAX = 200 * 1024;
 
 template <int WF, int ST, int PRO, int EPI>
@@ -339,6 +358,26 @@ int gemv_launch(const GemvPlan &plan, const GemvParams &p, int pro, int epi, cud
     LLMRS_GEMV_VARIANTS(LLMRS_GEMV_CASE)
 #undef LLMRS_GEMV_CASE
     return fail(LLMRS_ENOTSUP, "gemv: unsupported variant wf=%d st=%d pro=%d epi=%d", wf, st, pro, epi);
+}
+
+int gemv_norm_quantize(const float *x, const float *w, int K, float eps, int8_t *q, float *s, uint32_t *err,
+                       cudaStream_t stream)
+{
+    LLMRS_CHECK_ARG(x && w && q && s, "NULL argument");
+    LLMRS_CHECK_ARG(K > 0 && K % 32 == 0, "rms_norm_quantize: k=%d must be a positive multiple of 32", K);
+    LLMRS_CHECK_ARG(!((uintptr_t)x & 15) && !((uintptr_t)w & 15) && !((uintptr_t)q & 15),
+                    "rms_norm_quantize: x, w and q must be 16-byte aligned");
+    const size_t smem = (size_t)(K / 32) * 40 + 64;
+    LLMRS_CHECK_ARG(smem <= 48 * 1024, "rms_norm_quantize: k=%d too large", K);
+    GemvParams p{};
+    p.K = K;
+    p.x = x;
+    p.norm_w = w;
+    p.eps = eps;
+    p.err = err;
+    norm_quant_kernel<<<1, PRO_THREADS, smem, stream>>>(p, q, s);
+    LLMRS_CUDA_TRY(cudaGetLastError());
+    return LLMRS_OK;
 }
 
 int gemv_grid(const GemvPlan &plan)

@@ -83,6 +83,7 @@ struct GemvParams {
     int ar_index;          // all-reduce instance within the step (layer)
     int ar_per_step;       // instances of this kind per step
     int row_offset;        // EPI_ARGMAX: global index of local row 0
+    unsigned long long peer_ns; // longest wait for another rank's data (0: 5 s)
 };
 
 // Launch geometry + TMA descriptors of one weight matrix, built once per weight.
@@ -106,6 +107,9 @@ int gemv_launch(const GemvPlan &plan, const GemvParams &p, int pro, int epi, cud
 // set kernel attributes (dynamic smem limits) for every variant on the current device;
 // called once per context, outside any stream capture
 int gemv_prepare(void);
+// one row's RMSNorm + Q8_0 exactly as the GEMV prologue computes it (codes [K], scales [K/32])
+int gemv_norm_quantize(const float *x, const float *w, int K, float eps, int8_t *q, float *s, uint32_t *err,
+                       cudaStream_t stream);
 // CTAs a launch of this plan uses
 int gemv_grid(const GemvPlan &plan);
 // weight stages a GEMV streams before its activation loads are issued

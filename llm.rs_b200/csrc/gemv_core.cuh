@@ -319,7 +319,8 @@ __device__ __forceinline__ void load_activation(const GemvParams &p, uint32_t *a
     }
     // AR: the 4 partial values of rank q at off, once every word carries this
     // exchange's tag (each 8-byte word is written whole, so a matching tag
-    // means its value is the one sent); gives up after 5 s
+    // means its value is the one sent); gives up after p.peer_ns (default 5 s)
+    const uint64_t peer_ns = p.peer_ns ? p.peer_ns : 5000000000ull;
     auto ll_load4 = [&](int q, size_t off, float (&v)[4]) {
         const unsigned long long *src = part + (size_t)q * K + off;
         uint64_t t0 = 0;
@@ -337,7 +338,7 @@ __device__ __forceinline__ void load_activation(const GemvParams &p, uint32_t *a
                 const uint64_t now = globaltimer_ns();
                 if (spin == 0u)
                     t0 = now;
-                else if (now - t0 > 5000000000ull ||
+                else if (now - t0 > peer_ns ||
                          *reinterpret_cast<volatile uint32_t *>(p.err) == DEV_ERR_PEER_TIMEOUT) {
                     atomicCAS(p.err, 0u, (uint32_t)DEV_ERR_PEER_TIMEOUT);
                     v[0] = v[1] = v[2] = v[3] = 0.0f;
@@ -563,7 +564,8 @@ __device__ __forceinline__ void argmax_finalize(const GemvParams &p, unsigned lo
                 __threadfence_system();
                 for (int q = 0; q < tp->size; q++)
                     atomicAdd_system(tp->cnt[q] + TP_CNT_KEY, 1ull);
-                if (wait_counter(tp->cnt[tp->rank] + TP_CNT_KEY, (epoch + 1) * (unsigned long long)tp->size, p.err))
+                if (wait_counter(tp->cnt[tp->rank] + TP_CNT_KEY, (epoch + 1) * (unsigned long long)tp->size, p.err,
+                                 p.peer_ns ? p.peer_ns : 5000000000ull))
                     for (int q = 0; q < tp->size; q++) {
                         const unsigned long long k = __ldcg(tp->keys[tp->rank] + q);
                         best = k > best ? k : best;

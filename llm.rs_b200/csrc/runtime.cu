@@ -154,6 +154,7 @@ struct llmrs_model {
     TpLink *d_tp = nullptr;
     bool tp_connected = false;
     unsigned int *att_counter = nullptr;
+    unsigned long long peer_ns = 5000000000ull; // tensor parallel: longest wait for another rank
     StepState *state = nullptr;
     int *token_log = nullptr;
     int log_cap = 0;
@@ -534,6 +535,14 @@ int llmrs_quantize_row_q8_0(llmrs_ctx *ctx, const float *d_x, int8_t *d_q, float
     LLMRS_CHECK_ARG(ctx && d_x && d_q && d_s && rows >= 0 && k > 0 && k % 32 == 0,
                     "quantize_row_q8_0: bad arguments (k=%d must be a multiple of 32)", k);
     return op_quantize_q8(ctx->stream, d_x, d_q, d_s, (size_t)rows * (k / 32));
+}
+
+int llmrs_rms_norm_quantize_q8_0(llmrs_ctx *ctx, const float *d_x, const float *d_w, int8_t *d_q, float *d_s, int k,
+                                 float eps)
+{
+    LLMRS_CHECK_ARG(ctx, "NULL context");
+    LLMRS_TRY(gemv_norm_quantize(d_x, d_w, k, eps, d_q, d_s, ctx->d_err, ctx->stream));
+    return LLMRS_OK;
 }
 
 int llmrs_quantize_q4(llmrs_ctx *ctx, const float *d_w, size_t n, uint8_t *d_qs, float *d_scales)
@@ -1008,6 +1017,7 @@ static void build_ops(llmrs_model *m, std::vector<HostOp> &ops, unsigned long lo
         o.g = g;
         o.g.trace = trace;
         o.g.trace_slot = slot++;
+        o.g.peer_ns = m->peer_ns;
         o.pro = pro;
         o.epi = epi;
         ops.push_back(o);
@@ -1281,9 +1291,20 @@ static int prefill_weights_ready(llmrs_model *m, bool *ready)
                 for (int i = 0; i < 4; i++)
                     total += prefill_bf16_bytes(q[i]->n, q[i]->k);
             }
-            cudaError_t e = cudaMalloc(&m->pf_bf16, total);
-            if (e != cudaSuccess)
-                return fail(LLMRS_ENOMEM, "bf16 prefill weights (%zu bytes): %s", total, cudaGetErrorString(e));
+            // The copy is an optimisation: when it does not fit (or exceeds
+            // LLMRS_PREFILL_BF16_MAX_MB), the int8 tensor-core GEMM reads the
+            // Q8_0 / Q4_0 storage directly, with the same exact results.
+            const char *cap_env = getenv("LLMRS_PREFILL_BF16_MAX_MB");
+            const size_t cap = cap_env ? (size_t)atol(cap_env) << 20 : ~(size_t)0;
+            cudaError_t e = total <= cap ? cudaMalloc(&m->pf_bf16, total) : cudaErrorMemoryAllocation;
+            if (e != cudaSuccess) {
+                cudaGetLastError(); // clear the failed allocation's error state
+                m->pf_bf16 = nullptr;
+                m->pf_bf = 0;
+                m->pf_weights = ok;
+                *ready = m->pf_weights == 1;
+                return LLMRS_OK;
+            }
             uint8_t *b = reinterpret_cast<uint8_t *>(m->pf_bf16);
             for (int l = 0; l < m->cfg.n_layers; l++) {
                 LayerW &L = m->layers[l];
@@ -1454,7 +1475,8 @@ int llmrs_prefill(llmrs_model *m, const int *h_ids, int n, int start_pos, float 
         LLMRS_CUDA_TRY(cudaMemcpyAsync(m->pf_ids, h_ids, (size_t)n * 4, cudaMemcpyHostToDevice, s));
         LLMRS_TRY(prefill_rows(m, n, start_pos, h_ids[n - 1]));
     }
-    // Otherwise (Q4_0 weights, tensor parallel, short prompts): rows of a
+    // Otherwise (tensor parallel, short prompts, a linear whose K is not a
+    // multiple of 256): rows of a
     // prefill chunk are causal and row-independent in every contraction
     // (src/backend/cpu.rs:90-110, src/core/layer.rs:260-269), so the chunk
     // runs as n consecutive single-row steps over the same cache.
@@ -1697,6 +1719,52 @@ int llmrs_model_tp_connect(llmrs_model *m, void *const *regions)
     LLMRS_TRY(finish_sync(m));
     m->tp_connected = true;
     return LLMRS_OK;
+}
+
+int llmrs_model_set_peer_timeout(llmrs_model *m, int timeout_ms)
+{
+    LLMRS_CHECK_ARG(m, "model is NULL");
+    LLMRS_CHECK_ARG(timeout_ms >= 1 && timeout_ms <= 600000, "peer timeout %d ms outside [1, 600000]", timeout_ms);
+    cudaSetDevice(m->ctx->device);
+    LLMRS_TRY(finish_sync(m));
+    m->peer_ns = (unsigned long long)timeout_ms * 1000000ull;
+    // the step graphs hold the old limit: rebuild them on next use
+    if (m->graph)
+        cudaGraphExecDestroy(m->graph);
+    if (m->graph_traced)
+        cudaGraphExecDestroy(m->graph_traced);
+    m->graph = m->graph_traced = nullptr;
+    return LLMRS_OK;
+}
+
+int llmrs_model_tp_epoch(llmrs_model *m, unsigned long long *epoch)
+{
+    LLMRS_CHECK_ARG(m && epoch, "NULL argument");
+    cudaSetDevice(m->ctx->device);
+    LLMRS_TRY(finish_sync(m));
+    LLMRS_CUDA_TRY(cudaMemcpy(epoch, &m->state->epoch, sizeof(*epoch), cudaMemcpyDeviceToHost));
+    return LLMRS_OK;
+}
+
+int llmrs_model_tp_resync(llmrs_model *m, unsigned long long epoch)
+{
+    LLMRS_CHECK_ARG(m, "model is NULL");
+    LLMRS_CHECK_ARG(m->T > 1 && m->tp_connected, "tensor-parallel model is not connected to its peers");
+    cudaSetDevice(m->ctx->device);
+    cudaStream_t s = m->ctx->stream;
+    LLMRS_TRY(finish_sync(m));
+    // exchange tags derive from the epoch, so after this every rank tags the
+    // same step alike and a stale word never matches; this rank's arrival
+    // counters are what `epoch` completed steps leave behind
+    unsigned long long cnt[TP_CNT_N] = {};
+    cnt[TP_CNT_KEY] = epoch * (unsigned long long)m->T;
+    uint8_t *own = reinterpret_cast<uint8_t *>(m->tp_region);
+    LLMRS_CUDA_TRY(cudaMemcpyAsync(own + m->tp_off_cnt, cnt, sizeof(cnt), cudaMemcpyHostToDevice, s));
+    LLMRS_CUDA_TRY(cudaMemcpyAsync(&m->state->epoch, &epoch, sizeof(epoch), cudaMemcpyHostToDevice, s));
+    LLMRS_CUDA_TRY(cudaMemsetAsync(&m->state->key, 0, sizeof(m->state->key), s));
+    LLMRS_CUDA_TRY(cudaMemsetAsync(&m->state->done, 0, sizeof(m->state->done), s));
+    LLMRS_CUDA_TRY(cudaMemsetAsync(&m->state->err, 0, sizeof(m->state->err), s));
+    return finish_sync(m);
 }
 
 int llmrs_ipc_get_handle(const void *d_ptr, void *handle_out)

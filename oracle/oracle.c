@@ -569,6 +569,7 @@ struct orc_model {
     orc_layer *L;
     float *embed, *final_norm;
     orc_lin lm_head;
+    float *trace; /* optional: [2*n_layers+1][hidden] residuals entering each RMSNorm (last row) */
 };
 
 static void lin_alloc(orc_lin *l, size_t n, size_t k, int fmt)
@@ -845,11 +846,16 @@ int orc_model_forward_embeds(orc_model *m, const float *xin, int n, int start_po
     size_t sz = sizeof(float) * (size_t)n * H;
     float *x = (float *)malloc(sz), *hn = (float *)malloc(sz), *a = (float *)malloc(sz), *f = (float *)malloc(sz);
     memcpy(x, xin, sz);
+    const size_t last = (size_t)(n - 1) * H;
     for (int l = 0; l < c->n_layers; l++) {
         orc_layer *L = &m->L[l];
+        if (m->trace)
+            memcpy(m->trace + (size_t)(2 * l) * H, x + last, sizeof(float) * H);
         orc_rms_norm(x, L->attn_norm, hn, n, H, c->rms_eps);
         attention(m, L, hn, n, start_pos, a);
         orc_add_assign(a, x, (size_t)n * H); /* attn_out += x */
+        if (m->trace)
+            memcpy(m->trace + (size_t)(2 * l + 1) * H, a + last, sizeof(float) * H);
         orc_rms_norm(a, L->mlp_norm, hn, n, H, c->rms_eps);
         mlp(m, L, hn, n, f);
         orc_add_assign(f, a, (size_t)n * H); /* mlp_out += h */
@@ -857,7 +863,9 @@ int orc_model_forward_embeds(orc_model *m, const float *xin, int n, int start_po
         x = f;
         f = t;
     }
-    orc_rms_norm(x + (size_t)(n - 1) * H, m->final_norm, hn, 1, H, c->rms_eps);
+    if (m->trace)
+        memcpy(m->trace + (size_t)(2 * c->n_layers) * H, x + last, sizeof(float) * H);
+    orc_rms_norm(x + last, m->final_norm, hn, 1, H, c->rms_eps);
     lin_forward(&m->lm_head, hn, 1, logits_last);
     free(x);
     free(hn);
@@ -929,6 +937,8 @@ int orc_model_tensor(orc_model *m, int layer, int which, void **qs, void **scale
     *k = l->k;
     return 0;
 }
+
+void orc_model_set_trace(orc_model *m, float *buf) { m->trace = buf; }
 
 float *orc_model_kcache(orc_model *m, int layer) { return m->L[layer].kc; }
 float *orc_model_vcache(orc_model *m, int layer) { return m->L[layer].vc; }

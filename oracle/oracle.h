@@ -65,6 +65,10 @@ void orc_model_kv_fill_synthetic(orc_model *m, uint64_t seed, int n_pos);
 int orc_model_forward(orc_model *m, const int *ids, int n, int start_pos, float *logits_last);
 /* forward from caller-provided embeddings [n][hidden] (used by layer-level tests) */
 int orc_model_forward_embeds(orc_model *m, const float *x, int n, int start_pos, float *logits_last);
+/* record, in every later forward, the last row's residual stream entering each
+ * RMSNorm into buf[2*n_layers+1][hidden]: [2l] before layer l's attention norm,
+ * [2l+1] before its MLP norm, [2L] before the final norm (NULL stops) */
+void orc_model_set_trace(orc_model *m, float *buf);
 /* raw access for tests and uploads (reference layouts) */
 int orc_model_tensor(orc_model *m, int layer, int which, void **qs, void **scales, size_t *n_rows, size_t *k);
 float *orc_model_kcache(orc_model *m, int layer);

@@ -77,6 +77,7 @@ def lib():
             "orc_model_forward_embeds": (ci, [vp, F32P, ci, ci, F32P]),
             "orc_model_tensor": (ci, [vp, ci, ci, ctypes.POINTER(vp), ctypes.POINTER(vp),
                                       ctypes.POINTER(sz), ctypes.POINTER(sz)]),
+            "orc_model_set_trace": (None, [vp, F32P]),
             "orc_model_kcache": (F32P, [vp, ci]),
             "orc_model_vcache": (F32P, [vp, ci]),
             "orc_model_cache_heads": (sz, [vp]),
@@ -325,6 +326,23 @@ class Model:
         if rc != 0:
             raise ValueError("orc_model_forward failed: %d" % rc)
         return out
+
+    def forward_traced(self, ids, start_pos):
+        """forward(), also returning the last row's residual stream entering
+        each RMSNorm: [2*n_layers+1][hidden] (attention norm of layer l at 2l,
+        MLP norm at 2l+1, final norm last)."""
+        buf = np.zeros((2 * self.cfg["n_layers"] + 1, self.cfg["hidden"]), np.float32)
+        lib().orc_model_set_trace(self.h, _p(buf, F32P))
+        try:
+            logits = self.forward(ids, start_pos)
+        finally:
+            lib().orc_model_set_trace(self.h, None)
+        return logits, buf
+
+    def norm_weight(self, layer, which):
+        """attention (0) / MLP (1) RMSNorm weight of `layer`, or the final norm (layer -1)"""
+        w, _ = self.tensor(layer, W_FINAL_NORM if layer < 0 else (W_ATTN_NORM if which == 0 else W_MLP_NORM))
+        return np.asarray(w, np.float32).reshape(-1)
 
     def forward_embeds(self, x, start_pos):
         x = _f32(np.atleast_2d(x))

@@ -124,3 +124,25 @@ def test_config4_8b_q8_prefill(llmrs, ctx, orc):
     cfg = with_(CFG_8B, n_layers=2, weight_format=1, max_seq=512)
     prompt = [orc.synth_token(4, i, cfg["vocab"]) for i in range(160)]
     check_q8(compare_run(llmrs, ctx, orc, cfg, 4, prompt, 2), 160, (Q8_ROW_FRACTION, 0.0))
+
+
+def test_prefill_without_room_for_the_bf16_copy(llmrs, ctx, monkeypatch):
+    """When the bf16 copy of the weights does not fit (forced here with
+    LLMRS_PREFILL_BF16_MAX_MB=1, read when a model first prefills), the
+    tensor-core prefill runs the int8 GEMM straight from the Q4_0 storage:
+    no error, and the same exact contractions give the same logits."""
+    cfg = with_(CFG_8B, n_layers=2, max_seq=128)
+    ids = [(17 * i + 5) % cfg["vocab"] for i in range(40)]
+    monkeypatch.setenv("LLMRS_PREFILL_BF16_MAX_MB", "1")
+    a = llmrs.Model(ctx, cfg)
+    a.init_synthetic(9)
+    ta, la = a.prefill(ids, 0)
+    ta2, la2 = a.prefill(ids, 0)  # a later prefill reuses the decision, no retry
+    monkeypatch.delenv("LLMRS_PREFILL_BF16_MAX_MB")
+    b = llmrs.Model(ctx, cfg)
+    b.init_synthetic(9)
+    tb, lb = b.prefill(ids, 0)
+    a.close()
+    b.close()
+    assert ta == ta2 == tb
+    assert np.array_equal(la, la2) and np.array_equal(la, lb)

@@ -1,5 +1,6 @@
 """Tensor-parallel decode on 2, 4 and 8 GPUs (one process per GPU, shards
-connected over CUDA IPC / NVLink) against the single-device CPU oracle.  The
+connected over CUDA IPC / NVLink) against the single-device CPU oracle, on a
+small model and on 2-layer models of the 8B and 70B shapes (configs 3 and 5).  The
 o_proj and down_proj sums are split across ranks and added in rank order, so
 logits agree to rounding (same bounds as the single-GPU parity tests); greedy
 tokens must match (teacher-forced).  Each case is skipped on boxes with fewer
@@ -60,7 +61,8 @@ def oracle_run(orc, cfg, seed, prompt, n_decode, kv):
     return out, forced
 
 
-@pytest.mark.parametrize("world,shape", [(2, "small"), (2, "8b2"), (4, "8b2"), (8, "8b2")])
+@pytest.mark.parametrize("world,shape", [(2, "small"), (2, "8b2"), (4, "8b2"), (8, "8b2"), (2, "70b2"), (4, "70b2"),
+                                         (8, "70b2")])
 def test_tensor_parallel_decode_matches_oracle(orc, world, shape):
     if n_gpus() < world:
         pytest.skip("needs %d GPUs" % world)
@@ -68,10 +70,14 @@ def test_tensor_parallel_decode_matches_oracle(orc, world, shape):
         cfg = dict(n_layers=2, hidden=512, n_heads=8, n_kv_heads=2, head_dim=64, ffn=1024, vocab=1000,
                    max_seq=96, rms_eps=1e-5, rope_theta=500000.0, weight_format=0, tied_embeddings=1, scale_dtype=0)
         seed, prompt, n_dec, kv = 21, [5, 17, 900, 3], 6, 0
-    else:
+    elif shape == "8b2":
         cfg = dict(n_layers=2, hidden=4096, n_heads=32, n_kv_heads=8, head_dim=128, ffn=14336, vocab=128256,
                    max_seq=4352, rms_eps=1e-5, rope_theta=500000.0, weight_format=0, tied_embeddings=0, scale_dtype=0)
         seed, prompt, n_dec, kv = 3, [orc.synth_token(3, 0, 128256)], 3, 4096
+    else:  # the 70B shape (config 5): hidden 8192, 64 query / 8 KV heads, FFN 28672, KV 2048
+        cfg = dict(n_layers=2, hidden=8192, n_heads=64, n_kv_heads=8, head_dim=128, ffn=28672, vocab=128256,
+                   max_seq=2176, rms_eps=1e-5, rope_theta=500000.0, weight_format=0, tied_embeddings=0, scale_dtype=0)
+        seed, prompt, n_dec, kv = 5, [orc.synth_token(5, 0, 128256)], 3, 2048
     ref, forced = oracle_run(orc, cfg, seed, prompt, n_dec, kv)
     got = run_tp(world, dict(cfg=cfg, seed=seed, prompt=prompt, forced=forced, kv=kv))
     assert len(got) == len(ref)
