@@ -49,9 +49,11 @@ extern "C" {
 #define LLMRS_ENCCL 6      /* NCCL error */
 #define LLMRS_EDEVICE 7    /* device-side error word set (bad token id, bad position) */
 
-/* ---- dtypes for block scales ---- */
+/* ---- dtypes: block scales (LLMRS_F16 / LLMRS_F32); raw checkpoint tensors
+ *      of llmrs_model_load_weight (LLMRS_F32 / LLMRS_BF16) ---- */
 #define LLMRS_F16 0
 #define LLMRS_F32 1
+#define LLMRS_BF16 2
 
 /* ---- weight formats ---- */
 #define LLMRS_WFMT_Q4_0 0
@@ -222,15 +224,34 @@ typedef struct {
 #define LLMRS_W_EMBED 8      /* [vocab][hidden] f32 */
 #define LLMRS_W_FINAL_NORM 9 /* [hidden] f32 */
 #define LLMRS_W_LM_HEAD 10   /* [vocab][hidden] quantised (ignored when tied) */
+#define LLMRS_W_GATE 11      /* [ffn][hidden] quantised: gate_proj alone (the gate rows of LLMRS_W_GATE_UP) */
+#define LLMRS_W_UP 12        /* [ffn][hidden] quantised: up_proj alone (the up rows of LLMRS_W_GATE_UP) */
 
 int llmrs_model_create(llmrs_ctx *ctx, const llmrs_config *cfg, llmrs_model **out);
 int llmrs_model_destroy(llmrs_model *model);
 /* random-init every weight from `seed` with the documented synthetic recipe */
 int llmrs_model_init_synthetic(llmrs_model *model, uint64_t seed);
 /* upload one tensor in the reference layout (quantised: h_codes + h_scales as
- * f32; f32 tensors: h_codes is float*, h_scales NULL).  For the tied 1B head
- * the LM head is re-derived on the device with quantize_q4 of the embedding. */
+ * f32; f32 tensors: h_codes is float*, h_scales NULL), always the whole,
+ * unsharded tensor of the shapes listed with the which-codes: a tensor-parallel
+ * rank takes its own shard (its heads' rows of q/k/v, its columns of o_proj and
+ * down_proj, its FFN rows of gate/up, its vocab rows of the LM head; the full
+ * embedding and norms).  For the tied 1B head the LM head is re-derived on the
+ * device with quantize_q4 of the embedding. */
 int llmrs_model_set_weight(llmrs_model *model, int layer, int which, const void *h_codes, const float *h_scales);
+/* Load one checkpoint tensor as the reference's loader reads it
+ * (src/core/loader.rs:25-46 read_tensor: f32 or bf16, row-major [rows][cols],
+ * the layout of the safetensors file; dtype LLMRS_F32 or LLMRS_BF16), whole and
+ * unsharded as for llmrs_model_set_weight.  On the device: bf16 -> f32 (exact),
+ * then for the linears quantize_q4 (src/core/tensor.rs:102-167, f32 block
+ * scales; Q8_0 models: the Q8_0 block quantiser), with the loader's layout
+ * decisions: K/V kept at n_kv_heads rows (the reference replicates them per
+ * query head, loader.rs:62-98, which quantises to identical rows), gate and up
+ * accepted fused (LLMRS_W_GATE_UP, loader.rs:128-147) or as LLMRS_W_GATE /
+ * LLMRS_W_UP, and the tied LM head quantised from the embedding
+ * (loader.rs:186-190).  Quantize_q4 scales are rarely exact in f16: checkpoint
+ * models use scale_dtype LLMRS_F32 (else LLMRS_EINVAL). */
+int llmrs_model_load_weight(llmrs_model *model, int layer, int which, const void *h_data, int dtype);
 /* KV cache: h_k/h_v [n_kv_heads][n_pos][head_dim] f32 written at positions [0,n_pos) */
 int llmrs_kv_fill(llmrs_model *model, int layer, const float *h_k, const float *h_v, int n_pos);
 int llmrs_kv_fill_synthetic(llmrs_model *model, uint64_t seed, int n_pos);

@@ -23,10 +23,10 @@ _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libllmrs_cuda.so")
 
 OK, EINVAL, ENOMEM, ECUDA, ETIMEDOUT, ENOTSUP, ENCCL, EDEVICE = range(8)
-F16, F32 = 0, 1
+F16, F32, BF16 = 0, 1, 2
 WFMT_Q4_0, WFMT_Q8_0 = 0, 1
 (W_Q, W_K, W_V, W_O, W_GATE_UP, W_DOWN, W_ATTN_NORM, W_MLP_NORM, W_EMBED, W_FINAL_NORM,
- W_LM_HEAD) = range(11)
+ W_LM_HEAD, W_GATE, W_UP) = range(13)
 
 # every symbol include/llmrs_cuda.h declares (checked by tests/test_synth_and_capi.py)
 EXPORTS = [
@@ -37,7 +37,7 @@ EXPORTS = [
     "llmrs_matmul", "llmrs_matmul_slice", "llmrs_add_assign", "llmrs_silu_mul", "llmrs_rope_inplace",
     "llmrs_rms_norm", "llmrs_softmax", "llmrs_scale", "llmrs_copy_from", "llmrs_quantize_row_q8_0",
     "llmrs_quantize_q4", "llmrs_rms_norm_quantize_q8_0", "llmrs_model_create", "llmrs_model_destroy", "llmrs_model_init_synthetic",
-    "llmrs_model_set_weight", "llmrs_kv_fill", "llmrs_kv_fill_synthetic", "llmrs_kv_read",
+    "llmrs_model_set_weight", "llmrs_model_load_weight", "llmrs_kv_fill", "llmrs_kv_fill_synthetic", "llmrs_kv_read",
     "llmrs_decode_step", "llmrs_generate", "llmrs_prefill", "llmrs_model_logits", "llmrs_rope_table",
     "llmrs_model_decode_kernel_count", "llmrs_model_time_decode", "llmrs_model_time_prefill",
     "llmrs_model_profile_decode", "llmrs_time_gemv",
@@ -117,6 +117,7 @@ def lib():
         "llmrs_model_destroy": (ci, [vp]),
         "llmrs_model_init_synthetic": (ci, [vp, ctypes.c_uint64]),
         "llmrs_model_set_weight": (ci, [vp, ci, ci, vp, vp]),
+        "llmrs_model_load_weight": (ci, [vp, ci, ci, vp, ci]),
         "llmrs_kv_fill": (ci, [vp, ci, vp, vp, ci]),
         "llmrs_kv_fill_synthetic": (ci, [vp, ctypes.c_uint64, ci]),
         "llmrs_kv_read": (ci, [vp, ci, vp, vp, ci]),
@@ -446,6 +447,18 @@ class Model:
         check(lib().llmrs_model_set_weight(self.h, layer, which, _ptr(codes),
                                            None if sc is None else _ptr(sc)))
 
+    def load_weight(self, layer, which, data):
+        """One checkpoint tensor, whole and unsharded (llmrs_model_load_weight):
+        float32, or bfloat16 bits as uint16, in the safetensors layout."""
+        a = np.ascontiguousarray(data)
+        if a.dtype == np.float32:
+            dt = F32
+        elif a.dtype == np.uint16:
+            dt = BF16
+        else:
+            raise TypeError("load_weight takes float32 or bfloat16 bits (uint16), not %s" % a.dtype)
+        check(lib().llmrs_model_load_weight(self.h, int(layer), int(which), _ptr(a), dt))
+
     def kv_fill(self, layer, k, v):
         k = np.ascontiguousarray(k, np.float32)
         v = np.ascontiguousarray(v, np.float32)
@@ -577,6 +590,57 @@ class Model:
         check(lib().llmrs_model_time_prefill(self.h, _ptr(ids), ids.size, int(start_pos), int(iters),
                                              ctypes.byref(ms)))
         return ms.value
+
+
+def read_safetensors(path):
+    """{name: (array, dtype name)} of a safetensors file, memory-mapped: an
+    8-byte little-endian header length, a JSON header {name: {dtype, shape,
+    data_offsets}}, then the data.  BF16 tensors come back as their uint16 bits."""
+    import json
+    import struct
+    with open(path, "rb") as f:
+        n = struct.unpack("<Q", f.read(8))[0]
+        header = json.loads(f.read(n))
+    raw = np.memmap(path, np.uint8, mode="r", offset=8 + n)
+    kinds = {"F32": np.float32, "BF16": np.uint16}
+    out = {}
+    for name, meta in header.items():
+        if name == "__metadata__":
+            continue
+        if meta["dtype"] not in kinds:  # the reference's read_tensor bails the same way
+            raise ValueError("Unsupported dtype: %s (%s)" % (meta["dtype"], name))
+        b, e = meta["data_offsets"]
+        out[name] = (raw[b:e].view(kinds[meta["dtype"]]).reshape(meta["shape"]), meta["dtype"])
+    return out
+
+
+def load_safetensors(model, path):
+    """Load a Llama checkpoint into `model` with the reference's tensor names
+    and layout decisions (src/core/loader.rs:100-198): q/k/v/o, gate/up/down,
+    the two norms per layer, the embedding, the final norm and lm_head.weight
+    (absent: the LM head is quantize_q4 of the embedding, loader.rs:186-190).
+    Every tensor goes whole to llmrs_model_load_weight, which quantises it on
+    the device and keeps this rank's shard."""
+    t = read_safetensors(path)
+
+    def put(layer, which, name):
+        if name not in t:
+            raise KeyError("Tensor not found: %s" % name)
+        model.load_weight(layer, which, t[name][0])
+
+    put(-1, W_EMBED, "model.embed_tokens.weight")
+    for i in range(model.cfg["n_layers"]):
+        p = "model.layers.%d." % i
+        for which, name in ((W_Q, "self_attn.q_proj"), (W_K, "self_attn.k_proj"), (W_V, "self_attn.v_proj"),
+                            (W_O, "self_attn.o_proj"), (W_GATE, "mlp.gate_proj"), (W_UP, "mlp.up_proj"),
+                            (W_DOWN, "mlp.down_proj"), (W_ATTN_NORM, "input_layernorm"),
+                            (W_MLP_NORM, "post_attention_layernorm")):
+            put(i, which, p + name + ".weight")
+    put(-1, W_FINAL_NORM, "model.norm.weight")
+    if "lm_head.weight" in t:
+        put(-1, W_LM_HEAD, "lm_head.weight")
+    elif not model.cfg["tied_embeddings"]:
+        put(-1, W_LM_HEAD, "model.embed_tokens.weight")  # the reference's fallback: quantize_q4(embedding)
 
 
 def time_gemv(ctx, codes, scales, x, y, n, k, reps, fmt=WFMT_Q4_0, scale_dtype=F16):

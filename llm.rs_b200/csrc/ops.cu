@@ -319,9 +319,26 @@ __global__ void f32_to_f16_scales_kernel(const float *src, __half *dst, size_t n
     }
 }
 
+// bf16 -> f32 (the top 16 bits of the f32: exact, as half::bf16::to_f32,
+// src/core/loader.rs:37-41)
+__global__ void bf16_to_f32_kernel(const uint16_t *src, float *dst, size_t n)
+{
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        dst[i] = __uint_as_float((uint32_t)src[i] << 16);
+}
+
 } // namespace
 
 // ------------------------------------------------------------ host launchers
+int op_bf16_to_f32(cudaStream_t s, const uint16_t *src, float *dst, size_t n)
+{
+    if (n == 0)
+        return LLMRS_OK;
+    bf16_to_f32_kernel<<<ew_grid(n), EW_THREADS, 0, s>>>(src, dst, n);
+    LLMRS_CUDA_TRY(cudaGetLastError());
+    return LLMRS_OK;
+}
+
 int op_add_assign(cudaStream_t s, float *a, const float *b, size_t n)
 {
     add_assign_kernel<<<ew_grid(n), EW_THREADS, 0, s>>>(a, b, n);

@@ -18,6 +18,7 @@ int op_matmul_t(cudaStream_t s, const float *a, const float *b, float *c, int m,
 int op_matmul(cudaStream_t s, const float *a, const float *b, float *c, int m, int k, int n);
 int op_quantize_q8(cudaStream_t s, const float *x, int8_t *q, float *sc, size_t nblocks);
 int op_quantize_q4(cudaStream_t s, const float *w, size_t n, uint8_t *qs, float *scales);
+int op_bf16_to_f32(cudaStream_t s, const uint16_t *src, float *dst, size_t n);
 
 // synthetic quantised tensor: rows [row0,row0+nrows) x cols [col0,col0+ncols)
 // of the logical [.][K] tensor; destination row of source row r is

@@ -818,32 +818,64 @@ int llmrs_model_init_synthetic(llmrs_model *m, uint64_t seed)
     return finish_sync(m);
 }
 
-// upload n rows of a quantised tensor (reference layout) into dst rows
-// row*mul + add of a device tensor with the same k
-static int upload_quant(llmrs_model *m, const QW &q, const void *h_codes, const float *h_scales, size_t n, size_t k,
-                        int mul, int add)
+// Where a weight tensor of the reference layout goes in this rank's model:
+// rows [row0, row0 + n) x columns [col0, col0 + k) of the caller's full
+// [.][src_k] tensor land in rows add, add + mul, ... of the device tensor q
+// (q | k | v fused rows, gate / up interleaved, tensor-parallel shards).
+struct WeightSeg {
+    QW *q;
+    size_t n, k;
+    int mul, add;
+    size_t src_k, row0, col0;
+};
+
+static int weight_segs(llmrs_model *m, int layer, int which, WeightSeg *seg, int *nseg)
 {
-    cudaStream_t s = m->ctx->stream;
-    const size_t rb = m->wf == 0 ? k / 2 : k;
-    const size_t nb = k / 32;
-    LLMRS_CUDA_TRY(cudaMemcpy2DAsync(q.w + (size_t)add * rb, rb * mul, h_codes, rb, rb, n, cudaMemcpyHostToDevice, s));
-    if (q.st == LLMRS_F32) {
-        LLMRS_CUDA_TRY(cudaMemcpy2DAsync((uint8_t *)q.s + (size_t)add * nb * 4, nb * 4 * mul, h_scales, nb * 4,
-                                         nb * 4, n, cudaMemcpyHostToDevice, s));
+    const size_t T = (size_t)m->T, r = (size_t)m->rank, D = m->D, H = m->H, F = m->F, Vl = m->Vl;
+    const size_t qd = (size_t)m->Hq * D, kd = (size_t)m->Hkv * D;
+    *nseg = 1;
+    if (which == LLMRS_W_LM_HEAD) {
+        seg[0] = {&m->lm_head, Vl, H, 1, 0, H, r * Vl, 0};
         return LLMRS_OK;
     }
-    // f16 storage: stage the f32 scales, convert on device, check exactness
-    float *tmp = nullptr;
-    LLMRS_CUDA_TRY(cudaMallocAsync((void **)&tmp, n * nb * 4 + 16, s));
-    LLMRS_CUDA_TRY(cudaMemcpyAsync(tmp, h_scales, n * nb * 4, cudaMemcpyHostToDevice, s));
+    LLMRS_CHECK_ARG(layer >= 0 && layer < m->cfg.n_layers, "layer %d out of range", layer);
+    LayerW &L = m->layers[layer];
+    switch (which) {
+    case LLMRS_W_Q: seg[0] = {&L.qkv, qd, H, 1, 0, H, r * qd, 0}; break;
+    case LLMRS_W_K: seg[0] = {&L.qkv, kd, H, 1, (int)qd, H, r * kd, 0}; break;
+    case LLMRS_W_V: seg[0] = {&L.qkv, kd, H, 1, (int)(qd + kd), H, r * kd, 0}; break;
+    case LLMRS_W_O: seg[0] = {&L.o, H, qd, 1, 0, qd * T, 0, r * qd}; break;
+    case LLMRS_W_GATE_UP: // the reference's fused layout: gate rows [0, ffn), then up rows [ffn, 2 ffn)
+        seg[0] = {&L.gate_up, F, H, 2, 0, H, r * F, 0};
+        seg[1] = {&L.gate_up, F, H, 2, 1, H, F * T + r * F, 0};
+        *nseg = 2;
+        break;
+    case LLMRS_W_GATE: seg[0] = {&L.gate_up, F, H, 2, 0, H, r * F, 0}; break;
+    case LLMRS_W_UP: seg[0] = {&L.gate_up, F, H, 2, 1, H, r * F, 0}; break;
+    case LLMRS_W_DOWN: seg[0] = {&L.down, H, F, 1, 0, F * T, 0, r * F}; break;
+    default: return fail(LLMRS_EINVAL, "weight id %d is not a quantised linear", which);
+    }
+    return LLMRS_OK;
+}
+
+// f32 block scales [n][k/32] on the device into q's rows (add, add + mul, ...):
+// as they are, or as f16 when q stores f16 (every scale must then be exact)
+static int place_scales(llmrs_model *m, const WeightSeg &g, const float *d_s)
+{
+    cudaStream_t s = m->ctx->stream;
+    const size_t nb = g.k / 32;
+    if (g.q->st == LLMRS_F32) {
+        LLMRS_CUDA_TRY(cudaMemcpy2DAsync((uint8_t *)g.q->s + (size_t)g.add * nb * 4, nb * 4 * g.mul, d_s, nb * 4,
+                                         nb * 4, g.n, cudaMemcpyDeviceToDevice, s));
+        return LLMRS_OK;
+    }
     uint32_t *flag = m->ctx->d_err; // reuse the op error word as the inexact flag
     LLMRS_CUDA_TRY(cudaMemsetAsync(flag, 0, 4, s));
     __half *h16 = nullptr;
-    LLMRS_CUDA_TRY(cudaMallocAsync((void **)&h16, n * nb * 2 + 16, s));
-    LLMRS_TRY(scales_to_f16(s, tmp, h16, n * nb, flag));
-    LLMRS_CUDA_TRY(cudaMemcpy2DAsync((uint8_t *)q.s + (size_t)add * nb * 2, nb * 2 * mul, h16, nb * 2, nb * 2, n,
-                                     cudaMemcpyDeviceToDevice, s));
-    LLMRS_CUDA_TRY(cudaFreeAsync(tmp, s));
+    LLMRS_CUDA_TRY(cudaMallocAsync((void **)&h16, g.n * nb * 2 + 16, s));
+    LLMRS_TRY(scales_to_f16(s, d_s, h16, g.n * nb, flag));
+    LLMRS_CUDA_TRY(cudaMemcpy2DAsync((uint8_t *)g.q->s + (size_t)g.add * nb * 2, nb * 2 * g.mul, h16, nb * 2, nb * 2,
+                                     g.n, cudaMemcpyDeviceToDevice, s));
     LLMRS_CUDA_TRY(cudaFreeAsync(h16, s));
     uint32_t inexact = 0;
     LLMRS_CUDA_TRY(cudaMemcpyAsync(&inexact, flag, 4, cudaMemcpyDeviceToHost, s));
@@ -855,57 +887,151 @@ static int upload_quant(llmrs_model *m, const QW &q, const void *h_codes, const 
     return LLMRS_OK;
 }
 
+// quantised host tensor (reference layout, f32 scales) -> one segment
+static int upload_quant(llmrs_model *m, const WeightSeg &g, int wf, const void *h_codes, const float *h_scales)
+{
+    cudaStream_t s = m->ctx->stream;
+    const size_t rb = wbytes(wf, 1, g.k), src_rb = wbytes(wf, 1, g.src_k);
+    const size_t nb = g.k / 32, src_nb = g.src_k / 32;
+    const uint8_t *c = (const uint8_t *)h_codes + g.row0 * src_rb + wbytes(wf, 1, g.col0);
+    const float *sc = h_scales + g.row0 * src_nb + g.col0 / 32;
+    LLMRS_CUDA_TRY(cudaMemcpy2DAsync(g.q->w + (size_t)g.add * rb, rb * g.mul, c, src_rb, rb, g.n,
+                                     cudaMemcpyHostToDevice, s));
+    float *tmp = nullptr;
+    LLMRS_CUDA_TRY(cudaMallocAsync((void **)&tmp, g.n * nb * 4 + 16, s));
+    LLMRS_CUDA_TRY(cudaMemcpy2DAsync(tmp, nb * 4, sc, src_nb * 4, nb * 4, g.n, cudaMemcpyHostToDevice, s));
+    const int rc = place_scales(m, g, tmp);
+    cudaFreeAsync(tmp, s);
+    return rc;
+}
+
+// rows of a raw f32 / bf16 host tensor, the slice [row0, +n) x [col0, +k) of
+// [.][src_k], as f32 on the device (the caller frees *out with cudaFreeAsync)
+static int stage_raw(llmrs_model *m, const void *h, int dtype, size_t src_k, size_t row0, size_t col0, size_t n,
+                     size_t k, float **out)
+{
+    cudaStream_t s = m->ctx->stream;
+    const size_t es = dtype == LLMRS_BF16 ? 2 : 4;
+    void *raw = nullptr;
+    LLMRS_CUDA_TRY(cudaMallocAsync(&raw, n * k * es + 16, s));
+    LLMRS_CUDA_TRY(cudaMemcpy2DAsync(raw, k * es, (const uint8_t *)h + (row0 * src_k + col0) * es, src_k * es, k * es,
+                                     n, cudaMemcpyHostToDevice, s));
+    if (dtype == LLMRS_F32) {
+        *out = (float *)raw;
+        return LLMRS_OK;
+    }
+    float *f = nullptr;
+    LLMRS_CUDA_TRY(cudaMallocAsync((void **)&f, n * k * 4 + 16, s));
+    LLMRS_TRY(op_bf16_to_f32(s, (const uint16_t *)raw, f, n * k));
+    LLMRS_CUDA_TRY(cudaFreeAsync(raw, s));
+    *out = f;
+    return LLMRS_OK;
+}
+
+// raw f32 / bf16 host weights -> quantised (quantize_q4, src/core/tensor.rs:102-167,
+// or the Q8_0 block quantiser for Q8_0 models) into one segment
+static int load_quant(llmrs_model *m, const WeightSeg &g, int wf, const void *h, int dtype)
+{
+    cudaStream_t s = m->ctx->stream;
+    float *f = nullptr;
+    LLMRS_TRY(stage_raw(m, h, dtype, g.src_k, g.row0, g.col0, g.n, g.k, &f));
+    const size_t rb = wbytes(wf, 1, g.k), nb = g.k / 32;
+    uint8_t *codes = nullptr;
+    float *sc = nullptr;
+    LLMRS_CUDA_TRY(cudaMallocAsync((void **)&codes, g.n * rb + 16, s));
+    LLMRS_CUDA_TRY(cudaMallocAsync((void **)&sc, g.n * nb * 4 + 16, s));
+    // blocks of 32 never straddle a row (k % 32 == 0), so quantising the slice
+    // gives the slice of the full tensor's quantisation
+    int rc = wf == 0 ? op_quantize_q4(s, f, g.n * g.k, codes, sc)
+                     : op_quantize_q8(s, f, reinterpret_cast<int8_t *>(codes), sc, g.n * nb);
+    if (rc == LLMRS_OK) {
+        cudaError_t e = cudaMemcpy2DAsync(g.q->w + (size_t)g.add * rb, rb * g.mul, codes, rb, rb, g.n,
+                                          cudaMemcpyDeviceToDevice, s);
+        rc = e == cudaSuccess ? place_scales(m, g, sc) : fail(LLMRS_ECUDA, "weight copy: %s", cudaGetErrorString(e));
+    }
+    cudaFreeAsync(f, s);
+    cudaFreeAsync(codes, s);
+    cudaFreeAsync(sc, s);
+    return rc;
+}
+
+// f32 / bf16 host vector or matrix -> an f32 device tensor (norms, embedding);
+// the tied LM head is then re-derived from this rank's embedding rows
+static int load_f32(llmrs_model *m, int layer, int which, const void *h, int dtype)
+{
+    cudaStream_t s = m->ctx->stream;
+    const size_t H = m->H, V = m->V, Vl = m->Vl, r = m->rank;
+    float *dst = nullptr;
+    size_t n = H;
+    switch (which) {
+    case LLMRS_W_ATTN_NORM: dst = m->layers[layer].attn_norm; break;
+    case LLMRS_W_MLP_NORM: dst = m->layers[layer].mlp_norm; break;
+    case LLMRS_W_FINAL_NORM: dst = m->final_norm; break;
+    case LLMRS_W_EMBED: dst = m->embed; n = V * H; break;
+    default: return fail(LLMRS_EINVAL, "weight id %d is not an f32 tensor", which);
+    }
+    if (dtype == LLMRS_F32 && h) {
+        LLMRS_CUDA_TRY(cudaMemcpyAsync(dst, h, n * 4, cudaMemcpyHostToDevice, s));
+    } else {
+        float *f = nullptr;
+        LLMRS_TRY(stage_raw(m, h, dtype, n, 0, 0, 1, n, &f));
+        LLMRS_CUDA_TRY(cudaMemcpyAsync(dst, f, n * 4, cudaMemcpyDeviceToDevice, s));
+        LLMRS_CUDA_TRY(cudaFreeAsync(f, s));
+    }
+    if (which == LLMRS_W_EMBED && m->cfg.tied_embeddings) // src/core/loader.rs:186-190
+        LLMRS_TRY(op_quantize_q4(s, m->embed + r * Vl * H, Vl * H, m->lm_head.w, (float *)m->lm_head.s));
+    return LLMRS_OK;
+}
+
+static bool is_f32_weight(int which)
+{
+    return which == LLMRS_W_ATTN_NORM || which == LLMRS_W_MLP_NORM || which == LLMRS_W_EMBED ||
+           which == LLMRS_W_FINAL_NORM;
+}
+
 int llmrs_model_set_weight(llmrs_model *m, int layer, int which, const void *h_codes, const float *h_scales)
 {
     if (m)
         prefill_invalidate(m);
     LLMRS_CHECK_ARG(m && h_codes, "NULL argument");
-    if (m->T > 1)
-        return fail(LLMRS_ENOTSUP, "set_weight: tensor-parallel models are filled by init_synthetic");
     cudaSetDevice(m->ctx->device);
-    cudaStream_t s = m->ctx->stream;
-    const int D = m->D, H = m->H, F = m->F, V = m->V;
-    const size_t qd = (size_t)m->Hq * D, kd = (size_t)m->Hkv * D;
     const bool global = which == LLMRS_W_EMBED || which == LLMRS_W_FINAL_NORM || which == LLMRS_W_LM_HEAD;
     LLMRS_CHECK_ARG(global || (layer >= 0 && layer < m->cfg.n_layers), "layer %d out of range", layer);
-    const bool quant = which <= LLMRS_W_DOWN || which == LLMRS_W_LM_HEAD;
-    LLMRS_CHECK_ARG(!quant || h_scales, "quantised tensor needs scales");
-    switch (which) {
-    case LLMRS_W_Q: LLMRS_TRY(upload_quant(m, m->layers[layer].qkv, h_codes, h_scales, qd, H, 1, 0)); break;
-    case LLMRS_W_K: LLMRS_TRY(upload_quant(m, m->layers[layer].qkv, h_codes, h_scales, kd, H, 1, (int)qd)); break;
-    case LLMRS_W_V: LLMRS_TRY(upload_quant(m, m->layers[layer].qkv, h_codes, h_scales, kd, H, 1, (int)(qd + kd))); break;
-    case LLMRS_W_O: LLMRS_TRY(upload_quant(m, m->layers[layer].o, h_codes, h_scales, H, qd, 1, 0)); break;
-    case LLMRS_W_GATE_UP: {
-        // reference layout: gate rows [0,F), then up rows [F,2F) -> interleave
-        const size_t rb = m->wf == 0 ? (size_t)H / 2 : (size_t)H;
-        const uint8_t *c = (const uint8_t *)h_codes;
-        LLMRS_TRY(upload_quant(m, m->layers[layer].gate_up, c, h_scales, F, H, 2, 0));
-        LLMRS_TRY(upload_quant(m, m->layers[layer].gate_up, c + (size_t)F * rb, h_scales + (size_t)F * (H / 32), F, H, 2, 1));
-        break;
+    if (is_f32_weight(which)) {
+        LLMRS_TRY(load_f32(m, layer, which, h_codes, LLMRS_F32));
+        return finish_sync(m);
     }
-    case LLMRS_W_DOWN: LLMRS_TRY(upload_quant(m, m->layers[layer].down, h_codes, h_scales, H, F, 1, 0)); break;
-    case LLMRS_W_ATTN_NORM:
-        LLMRS_CUDA_TRY(cudaMemcpyAsync(m->layers[layer].attn_norm, h_codes, (size_t)H * 4, cudaMemcpyHostToDevice, s));
-        break;
-    case LLMRS_W_MLP_NORM:
-        LLMRS_CUDA_TRY(cudaMemcpyAsync(m->layers[layer].mlp_norm, h_codes, (size_t)H * 4, cudaMemcpyHostToDevice, s));
-        break;
-    case LLMRS_W_EMBED:
-        LLMRS_CUDA_TRY(cudaMemcpyAsync(m->embed, h_codes, (size_t)V * H * 4, cudaMemcpyHostToDevice, s));
-        if (m->cfg.tied_embeddings) // src/core/loader.rs:186-190
-            LLMRS_TRY(op_quantize_q4(s, m->embed, (size_t)V * H, m->lm_head.w, (float *)m->lm_head.s));
-        break;
-    case LLMRS_W_FINAL_NORM:
-        LLMRS_CUDA_TRY(cudaMemcpyAsync(m->final_norm, h_codes, (size_t)H * 4, cudaMemcpyHostToDevice, s));
-        break;
-    case LLMRS_W_LM_HEAD:
-        if (m->cfg.tied_embeddings)
-            return LLMRS_OK; // derived from the embedding
-        LLMRS_TRY(upload_quant(m, m->lm_head, h_codes, h_scales, V, H, 1, 0));
-        break;
-    default:
-        return fail(LLMRS_EINVAL, "unknown weight id %d", which);
+    LLMRS_CHECK_ARG(h_scales, "quantised tensor needs scales");
+    if (which == LLMRS_W_LM_HEAD && m->cfg.tied_embeddings)
+        return LLMRS_OK; // derived from the embedding
+    WeightSeg seg[2];
+    int nseg = 0;
+    LLMRS_TRY(weight_segs(m, layer, which, seg, &nseg));
+    for (int i = 0; i < nseg; i++)
+        LLMRS_TRY(upload_quant(m, seg[i], m->wf, h_codes, h_scales));
+    return finish_sync(m);
+}
+
+int llmrs_model_load_weight(llmrs_model *m, int layer, int which, const void *h_data, int dtype)
+{
+    if (m)
+        prefill_invalidate(m);
+    LLMRS_CHECK_ARG(m && h_data, "NULL argument");
+    LLMRS_CHECK_ARG(dtype == LLMRS_F32 || dtype == LLMRS_BF16, "dtype %d is neither LLMRS_F32 nor LLMRS_BF16", dtype);
+    cudaSetDevice(m->ctx->device);
+    const bool global = which == LLMRS_W_EMBED || which == LLMRS_W_FINAL_NORM || which == LLMRS_W_LM_HEAD;
+    LLMRS_CHECK_ARG(global || (layer >= 0 && layer < m->cfg.n_layers), "layer %d out of range", layer);
+    if (is_f32_weight(which)) {
+        LLMRS_TRY(load_f32(m, layer, which, h_data, dtype));
+        return finish_sync(m);
     }
+    if (which == LLMRS_W_LM_HEAD && m->cfg.tied_embeddings)
+        return LLMRS_OK; // derived from the embedding
+    WeightSeg seg[2];
+    int nseg = 0;
+    LLMRS_TRY(weight_segs(m, layer, which, seg, &nseg));
+    for (int i = 0; i < nseg; i++)
+        LLMRS_TRY(load_quant(m, seg[i], m->wf, h_data, dtype));
     return finish_sync(m);
 }
 

@@ -371,6 +371,35 @@ class Model:
         scales = np.ctypeslib.as_array(ctypes.cast(sc, F32P), shape=(n * k // 32,)).copy()
         return codes, scales
 
+    def set_tensor(self, layer, which, codes, scales=None):
+        """Overwrite one of the model's tensors in place (the layout tensor()
+        returns: quantised codes + f32 scales, or an f32 vector/matrix), e.g.
+        with the quantised weights of a checkpoint."""
+        qs = ctypes.c_void_p()
+        sc = ctypes.c_void_p()
+        n = ctypes.c_size_t()
+        k = ctypes.c_size_t()
+        rc = lib().orc_model_tensor(self.h, layer, which, ctypes.byref(qs), ctypes.byref(sc),
+                                    ctypes.byref(n), ctypes.byref(k))
+        if rc != 0:
+            raise ValueError("bad tensor")
+        c = np.ascontiguousarray(codes)
+        size = n.value * k.value
+        if not sc.value:
+            want = size * 4
+        elif self.cfg["weight_format"] == 0 or (which == W_LM_HEAD and self.cfg["tied_embeddings"]):
+            want = size // 2
+        else:
+            want = size
+        if c.nbytes != want:
+            raise ValueError("tensor %d of layer %d takes %d bytes, got %d" % (which, layer, want, c.nbytes))
+        ctypes.memmove(qs.value, c.ctypes.data, want)
+        if sc.value:
+            s32 = np.ascontiguousarray(scales, np.float32)
+            if s32.size != size // 32:
+                raise ValueError("scales of tensor %d: %d values, need %d" % (which, s32.size, size // 32))
+            ctypes.memmove(sc.value, s32.ctypes.data, s32.nbytes)
+
     def kcache(self, layer):
         c = self.cfg
         heads = lib().orc_model_cache_heads(self.h)

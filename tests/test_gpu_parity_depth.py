@@ -18,9 +18,12 @@ bit.
             LM head is quantize_q4 of an N(1, 0.02) embedding, so every logit
             is near the sum of the final hidden state (|logit| ~ 2100) and one
             ulp there is 1.2e-4: the max-abs bound is applied to the logits
-            divided by max|logit| / 100 (a relative 2e-4), and
-            test_config1_prologue_flips measures, layer by layer, the flipped
-            Q8_0 codes that produce the difference.
+            divided by max|logit| / 100 (a relative 2e-4).
+            test_config1_prologue_flips measures, layer by layer, how many
+            Q8_0 codes the GPU's fused RMSNorm + Q8_0 prologue alone changes on
+            the reference's own residual stream: none (measured on B200), so
+            the remaining difference enters through attention's reordered
+            softmax / P.V sums.
   config 4  8B shape with Q8_0 linears: a 512-token prompt + 64 decode steps.
             Its synthetic codes are uniform in -127..127, so every linear
             amplifies a perturbation ~7x and one flipped activation code moves
@@ -111,9 +114,10 @@ def test_config1_prologue_flips(llmrs, ctx, orc, be):
     """Per layer, the Q8_0 codes that the decode GEMVs' fused RMSNorm + Q8_0
     prologue gives for the oracle's own residual stream (after the config-1
     prompt), against CpuBackend::rms_norm + quantize_row_q8_0 of the same
-    input: all but a few codes per layer are identical, each differing one is
-    off by exactly 1 (a value at a rounding boundary of the quantiser), and the
-    block scales agree to a few ulps."""
+    input: any differing code is off by exactly 1 (a value at a rounding
+    boundary of the quantiser), at most one code in a thousand differs
+    (measured on B200: none in the 33 norms), and the block scales agree to a
+    few ulps."""
     cfg = CFG_1B
     om = orc.Model(cfg)
     om.init_synthetic(1)

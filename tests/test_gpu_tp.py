@@ -61,6 +61,39 @@ def oracle_run(orc, cfg, seed, prompt, n_decode, kv):
     return out, forced
 
 
+def test_tensor_parallel_checkpoint_ingest(orc, tmp_path):
+    """Every rank loads the same safetensors checkpoint (llmrs_model_load_weight
+    keeps its own shard); the ranks together match the oracle holding the
+    reference loader's quantised weights."""
+    world = 2
+    if n_gpus() < world:
+        pytest.skip("needs %d GPUs" % world)
+    from test_gpu_ingest import CFG, make_checkpoint, reference_tensors, write_safetensors
+    cfg = dict(CFG)
+    stored, seen = make_checkpoint(cfg, 5, "BF16")
+    path = str(tmp_path / "tp.safetensors")
+    write_safetensors(path, stored)
+    om = orc.Model(cfg)
+    om.init_synthetic(0)
+    for layer, which, codes, scales in reference_tensors(orc, cfg, seen):
+        om.set_tensor(layer, which, codes, scales)
+    prompt, n_dec = [5, 17, 900, 3], 4
+    ref = [om.forward(prompt, 0)]
+    forced, pos = [], len(prompt)
+    for _ in range(n_dec):
+        forced.append(int(orc.argmax(ref[-1])))
+        ref.append(om.forward([forced[-1]], pos))
+        pos += 1
+    om.close()
+    got = run_tp(world, dict(cfg=cfg, seed=0, prompt=prompt, forced=forced, kv=0, ckpt=path))
+    assert len(got) == len(ref)
+    for step, (g, o) in enumerate(zip(got, ref)):
+        gl = np.asarray(g["logits"], np.float32)
+        assert len(set(g["tokens"])) == 1 and (g["tokens"][0] == orc.argmax(o) or orc.top2_margin(o) < 1e-3)
+        rel = float(np.linalg.norm((gl - o).astype(np.float64)) / np.linalg.norm(o.astype(np.float64)))
+        assert float(np.abs(gl - o).max()) < LOGIT_ABS and rel < LOGIT_REL_L2, (step, rel)
+
+
 @pytest.mark.parametrize("world,shape", [(2, "small"), (2, "8b2"), (4, "8b2"), (8, "8b2"), (2, "70b2"), (4, "70b2"),
                                          (8, "70b2")])
 def test_tensor_parallel_decode_matches_oracle(orc, world, shape):

@@ -1,5 +1,5 @@
 """One rank of a tensor-parallel decode run (launched by tests/test_gpu_tp.py
-through torch.distributed.run): builds this rank's shard of a synthetic model,
+through torch.distributed.run): builds this rank's shard of a synthetic model (or loads it from a checkpoint),
 connects to the other ranks over CUDA IPC, runs a prompt and teacher-forced
 decode steps, and rank 0 prints every step's token and the full logits
 (rank shards concatenated in rank order) as one JSON line."""
@@ -35,7 +35,10 @@ def main():
     ctx = L.Context(local)
     cfg = dict(spec["cfg"], tp_rank=rank, tp_size=world)
     m = L.Model(ctx, cfg)
-    m.init_synthetic(spec["seed"])
+    if spec.get("ckpt"):  # every rank reads the whole checkpoint and keeps its shard
+        L.load_safetensors(m, spec["ckpt"])
+    else:
+        m.init_synthetic(spec["seed"])
     kv = spec.get("kv", 0)
     if kv:
         m.kv_fill_synthetic(spec["seed"], kv)
