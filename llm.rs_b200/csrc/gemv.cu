@@ -43,7 +43,11 @@ namespace llmrs {
 
 namespace {
 
-template <int WF, int ST, int PRO, int EPI>
+// One binary per (weight format, scale format): the prologue and epilogue are
+// run-time choices (p.pro, p.epi), so the five GEMVs of a decode layer run the
+// same code and keep it in the SM's instruction cache from launch to launch
+// (one instantiation per variant made every launch refetch its code).
+template <int WF, int ST>
 __global__ void __launch_bounds__(NTHREADS, 1)
     gemv_tma_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap ts, const GemvParams p)
 {
@@ -100,7 +104,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
     const int ctid = threadIdx.x;
     uint32_t cpar = 0, lpar = 0;
-    gemv_consume<WF, ST, PRO, EPI>(p, w, sm, cpar, lpar, ctid, true); // waits for the previous kernel itself
+    gemv_consume<WF, ST>(p, p.pro, p.epi, w, sm, cpar, lpar, ctid, true); // waits for the previous kernel itself
     LLMRS_TRACE_FLUSH(0);
     if (ctid == 0)
         trace_end(p.trace, p.trace_slot);
@@ -121,7 +125,7 @@ __global__ void __launch_bounds__(SIMPLE_THREADS) gemv_simple_kernel(const GemvP
     int *act_c = reinterpret_cast<int *>(act_s + nb);
     float *red = reinterpret_cast<float *>(act_c + nb);
     griddep_wait();
-    load_activation<WF, PRO>(p, act, act_s, act_c, red, threadIdx.x, SIMPLE_THREADS, 1, nullptr);
+    load_activation<WF>(p, PRO, act, act_s, act_c, red, threadIdx.x, SIMPLE_THREADS, 1, nullptr);
     named_bar_sync(1, SIMPLE_THREADS);
     const int row = blockIdx.x * blockDim.x + threadIdx.x;
     unsigned long long best = 0ull;
@@ -194,7 +198,7 @@ __global__ void __launch_bounds__(PRO_THREADS) norm_quant_kernel(const GemvParam
     float *act_s = reinterpret_cast<float *>(smem + (size_t)nb * 32);
     int *act_c = reinterpret_cast<int *>(act_s + nb);
     float *red = reinterpret_cast<float *>(act_c + nb);
-    load_activation<1, PRO_NORM>(p, act, act_s, act_c, red, threadIdx.x, PRO_THREADS, 1, nullptr);
+    load_activation<1>(p, PRO_NORM, act, act_s, act_c, red, threadIdx.x, PRO_THREADS, 1, nullptr);
     named_bar_sync(1, PRO_THREADS);
     for (int i = threadIdx.x; i < nb * 8; i += PRO_THREADS)
         reinterpret_cast<uint32_t *>(q)[i] = act[i];
@@ -204,29 +208,42 @@ __global__ void __launch_bounds__(PRO_THREADS) norm_quant_kernel(const GemvParam
 
 constexpr int SIMPLE_SMEM_MAX = 200 * 1024;
 
+template <int WF, int ST>
+cudaError_t prepare_fast()
+{
+    return cudaFuncSetAttribute(gemv_tma_kernel<WF, ST>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)SMEM_BUDGET + 2048);
+}
+
 template <int WF, int ST, int PRO, int EPI>
 cudaError_t prepare_one()
 {
-    cudaError_t e = cudaFuncSetAttribute(gemv_tma_kernel<WF, ST, PRO, EPI>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BUDGET + 2048);
-    if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(gemv_simple_kernel<WF, ST, PRO, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 SIMPLE_SMEM_MAX);
-    return e;
+    return cudaFuncSetAttribute(gemv_simple_kernel<WF, ST, PRO, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                SIMPLE_SMEM_MAX);
+}
+
+template <int WF, int ST>
+int launch_fast(const GemvPlan &plan, const GemvParams &p0, int pro, int epi, cudaStream_t stream, bool pdl)
+{
+    GemvParams p = p0;
+    p.pro = pro;
+    p.epi = epi;
+    p.n_stages = plan.stages;
+    p.n_pre = gemv_prefetch_stages();
+    p.box_rows = plan.box_rows;
+    p.rows_per_cta = plan.rows_per_cta;
+    LLMRS_CUDA_TRY(launch(gemv_tma_kernel<WF, ST>, dim3(plan.grid), dim3(NTHREADS), plan.smem, stream, pdl, plan.tw,
+                          plan.ts, p));
+    return LLMRS_OK;
 }
 
 template <int WF, int ST, int PRO, int EPI>
 int launch_one(const GemvPlan &plan, const GemvParams &p0, cudaStream_t stream, bool pdl)
 {
     GemvParams p = p0;
-    if (plan.fast) {
-        p.n_stages = plan.stages;
-        p.n_pre = gemv_prefetch_stages();
-        p.box_rows = plan.box_rows;
-        p.rows_per_cta = plan.rows_per_cta;
-        LLMRS_CUDA_TRY(launch(gemv_tma_kernel<WF, ST, PRO, EPI>, dim3(plan.grid), dim3(NTHREADS), plan.smem, stream,
-                              pdl, plan.tw, plan.ts, p));
-    } else {
+    p.pro = PRO;
+    p.epi = EPI;
+    {
         const int nb = p.K / 32;
         size_t smem = (size_t)nb * 40 + 64;
         LLMRS_CHECK_ARG(smem <= (size_t)SIMPLE_SMEM_MAX, "gemv: K=%d too large", p.K);
@@ -352,6 +369,22 @@ int gemv_launch(const GemvPlan &plan, const GemvParams &p, int pro, int epi, cud
     LLMRS_CHECK_ARG(p.N == plan.N && p.K == plan.K, "gemv: params do not match the plan");
     LLMRS_CHECK_ARG(epi != EPI_SILU || p.N % 2 == 0, "gemv: SiLU epilogue needs an even row count");
     const int wf = plan.wf, st = plan.st;
+    bool known = false; // a variant the library instantiates (the fast kernel takes any of them at run time)
+#define LLMRS_GEMV_KNOWN(WF, ST, PRO, EPI)                                                                  \
+    if (pro == PRO && epi == EPI)                                                                          \
+        known = true;
+    LLMRS_GEMV_VARIANTS(LLMRS_GEMV_KNOWN)
+#undef LLMRS_GEMV_KNOWN
+    if (plan.fast && known) {
+        if (wf == 0 && st == 0)
+            return launch_fast<0, 0>(plan, p, pro, epi, stream, pdl);
+        if (wf == 0 && st == 1)
+            return launch_fast<0, 1>(plan, p, pro, epi, stream, pdl);
+        if (wf == 1 && st == 0)
+            return launch_fast<1, 0>(plan, p, pro, epi, stream, pdl);
+        if (wf == 1 && st == 1)
+            return launch_fast<1, 1>(plan, p, pro, epi, stream, pdl);
+    }
 #define LLMRS_GEMV_CASE(WF, ST, PRO, EPI)                                                                   \
     if (wf == WF && st == ST && pro == PRO && epi == EPI)                                                  \
         return launch_one<WF, ST, PRO, EPI>(plan, p, stream, pdl);
@@ -397,7 +430,13 @@ int gemv_prefetch_stages(void)
 
 int gemv_prepare(void)
 {
-    cudaError_t e = cudaSuccess;
+    cudaError_t e = prepare_fast<0, 0>();
+    if (e == cudaSuccess)
+        e = prepare_fast<0, 1>();
+    if (e == cudaSuccess)
+        e = prepare_fast<1, 0>();
+    if (e == cudaSuccess)
+        e = prepare_fast<1, 1>();
 #define LLMRS_GEMV_PREP(WF, ST, PRO, EPI)                                                                   \
     if (e == cudaSuccess)                                                                                  \
         e = prepare_one<WF, ST, PRO, EPI>();

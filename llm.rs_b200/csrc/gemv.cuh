@@ -84,6 +84,7 @@ struct GemvParams {
     int ar_per_step;       // instances of this kind per step
     int row_offset;        // EPI_ARGMAX: global index of local row 0
     unsigned long long peer_ns; // longest wait for another rank's data (0: 5 s)
+    int pro, epi;          // GemvPro / GemvEpi of this launch (set by gemv_launch)
 };
 
 // Launch geometry + TMA descriptors of one weight matrix, built once per weight.

@@ -257,19 +257,25 @@ __device__ __forceinline__ void st_volatile_u64(unsigned long long *a, unsigned 
 
 // dep_wait: this thread has not yet waited for the previous kernel; the loads
 // that do not depend on it (RMSNorm weights) are issued first, then the wait.
-template <int WF, int PRO>
-__device__ __forceinline__ void load_activation(const GemvParams &p, uint32_t *act, float *act_s, int *act_c, float *red, int tid,
-                                int nthr, int bar, uint64_t *issued, bool dep_wait = false)
+// `pro` is a GemvPro: a run-time value in the decode kernel (one binary serves
+// every prologue, so the step's kernels share their code in the instruction
+// cache), a constant where a caller inlines it for one prologue.
+template <int WF>
+__device__ __forceinline__ void load_activation(const GemvParams &p, const int pro, uint32_t *act, float *act_s,
+                                                int *act_c, float *red, int tid, int nthr, int bar, uint64_t *issued,
+                                                bool dep_wait = false)
 {
     const int K = p.K, nb = K >> 5;
     const bool has = tid < nb;
-    constexpr bool EARLY_W = PRO == PRO_NORM || PRO == PRO_EMBED_NORM; // norm weights loaded before the wait
+    const bool NORM = pro == PRO_NORM || pro == PRO_EMBED_NORM || pro == PRO_AR_NORM;
+    const bool AR = pro == PRO_AR_NORM;
+    const bool EARLY_W = pro == PRO_NORM || pro == PRO_EMBED_NORM; // norm weights loaded before the wait
     if (!EARLY_W && dep_wait) {
         griddep_wait();
         if (tid == 0)
             trace_go(p.trace, p.trace_slot);
     }
-    if (PRO == PRO_Q8) {
+    if (pro == PRO_Q8) {
         uint4 c0 = make_uint4(0, 0, 0, 0), c1 = c0;
         float xs = 0.0f;
         if (has) {
@@ -290,14 +296,15 @@ __device__ __forceinline__ void load_activation(const GemvParams &p, uint32_t *a
         }
         return;
     }
-    constexpr bool NORM = PRO == PRO_NORM || PRO == PRO_EMBED_NORM || PRO == PRO_AR_NORM;
-    constexpr bool AR = PRO == PRO_AR_NORM;
-    constexpr int ACT_ROUNDS = NORM ? 4 : 8;
+    // Register buffer of 8 rounds: x in rounds [0, XR); with a norm, its
+    // weights for rounds 0..3 sit in buf[4..7].
+    constexpr int NBUF = 8;
+    const int XR = NORM ? 4 : 8;
     const int warp = tid >> 5, lane = tid & 31, sub = lane >> 3, j = lane & 7;
     const int nwarps = nthr >> 5;
     const int rounds = (nb + 4 * nwarps - 1) / (4 * nwarps);
     const float *x = p.x;
-    if (PRO == PRO_EMBED_NORM) {
+    if (pro == PRO_EMBED_NORM) {
         int tok = p.state->token;
         if (tok < 0 || tok >= p.vocab) {
             if (tid == 0)
@@ -356,7 +363,7 @@ __device__ __forceinline__ void load_activation(const GemvParams &p, uint32_t *a
         u[1] = t.y;
         u[2] = t.z;
         u[3] = t.w;
-        if (AR) { // the ranks' partial sums in rank order, then + x
+        if (AR) {
             float s[4], w[4];
             ll_load4(0, off, s);
             for (int q = 1; q < nparts; q++) {
@@ -377,14 +384,14 @@ __device__ __forceinline__ void load_activation(const GemvParams &p, uint32_t *a
         u[2] = t.z;
         u[3] = t.w;
     };
-    const bool store_x = (PRO == PRO_EMBED_NORM || AR) && blockIdx.x == 0; // the residual stream's new value
-    float xv[ACT_ROUNDS][4], wv[NORM ? ACT_ROUNDS : 1][4];
+    const bool store_x = (pro == PRO_EMBED_NORM || AR) && blockIdx.x == 0; // the residual stream's new value
+    float buf[NBUF][4];
     if (NORM) { // the RMSNorm weights do not depend on the previous kernel
 #pragma unroll
-        for (int r = 0; r < ACT_ROUNDS; r++) {
+        for (int r = 0; r < 4; r++) {
             const int b = (r * nwarps + warp) * 4 + sub;
             if (r < rounds && b < nb)
-                load4w(b, wv[NORM ? r : 0]);
+                load4w(b, buf[4 + r]);
         }
         if (EARLY_W && dep_wait) {
             griddep_wait();
@@ -392,14 +399,30 @@ __device__ __forceinline__ void load_activation(const GemvParams &p, uint32_t *a
                 trace_go(p.trace, p.trace_slot);
         }
     }
+    if (AR) { // spins on peers' words: one rolled copy of that code
+#pragma unroll 1
+        for (int r = 0; r < 4 && r < rounds; r++) {
+            const int b = (r * nwarps + warp) * 4 + sub;
+            if (b < nb) {
+                float u[4];
+                load4(b, u);
 #pragma unroll
-    for (int r = 0; r < ACT_ROUNDS; r++) {
-        const int b = (r * nwarps + warp) * 4 + sub;
-        if (r < rounds && b < nb)
-            load4(b, xv[r]);
-    }
-    if (!AR)
+                for (int i = 0; i < 4; i++)
+#pragma unroll
+                    for (int q = 0; q < 4; q++)
+                        if (q == r)
+                            buf[q][i] = u[i];
+            }
+        }
+    } else {
+#pragma unroll
+        for (int r = 0; r < NBUF; r++) {
+            const int b = (r * nwarps + warp) * 4 + sub;
+            if (r < XR && r < rounds && b < nb)
+                load4(b, buf[r]);
+        }
         signal_issued(issued, tid);
+    }
     float scale = 1.0f;
     if (NORM) {
         // sum of squares in a fixed order: per lane, per warp (tree), warps in order
@@ -410,10 +433,11 @@ __device__ __forceinline__ void load_activation(const GemvParams &p, uint32_t *a
                 ss = __fadd_rn(ss, __fmul_rn(u[i], u[i]));
         };
 #pragma unroll
-        for (int r = 0; r < ACT_ROUNDS; r++)
+        for (int r = 0; r < 4; r++)
             if (r < rounds && (r * nwarps + warp) * 4 + sub < nb)
-                add_ss(xv[r]);
-        for (int r = ACT_ROUNDS; r < rounds; r++) {
+                add_ss(buf[r]);
+#pragma unroll 1
+        for (int r = XR; r < rounds; r++) {
             const int b = (r * nwarps + warp) * 4 + sub;
             if (b < nb) {
                 float u[4];
@@ -442,22 +466,32 @@ __device__ __forceinline__ void load_activation(const GemvParams &p, uint32_t *a
                 u[i] = __fmul_rn(__fmul_rn(u[i], scale), wn[i]);
         quantize_block8<WF>(u, j, live, act + (size_t)b * 8, act_s + b, act_c + b);
     };
-#pragma unroll
-    for (int r = 0; r < ACT_ROUNDS; r++) {
+    // one rolled copy of the quantiser: round r's registers are picked by value
+#pragma unroll 1
+    for (int r = 0; r < XR && r < rounds; r++) {
         const int b0 = (r * nwarps + warp) * 4;
-        if (r < rounds && b0 < nb) { // warp-uniform
-            const int b = b0 + sub;
-            const bool live = b < nb;
-            float u[4], wn[4];
+        if (b0 >= nb)
+            break; // warp-uniform
+        const int b = b0 + sub;
+        const bool live = b < nb;
+        float u[4] = {0.0f, 0.0f, 0.0f, 0.0f}, wn[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-            for (int i = 0; i < 4; i++) {
-                u[i] = live ? xv[r][i] : 0.0f;
-                wn[i] = live && NORM ? wv[NORM ? r : 0][i] : 0.0f;
-            }
-            finish(b, live, u, wn);
-        }
+        for (int q = 0; q < NBUF; q++)
+            if (q == r)
+#pragma unroll
+                for (int i = 0; i < 4; i++)
+                    u[i] = live ? buf[q][i] : 0.0f;
+        if (NORM)
+#pragma unroll
+            for (int q = 0; q < 4; q++)
+                if (q == r)
+#pragma unroll
+                    for (int i = 0; i < 4; i++)
+                        wn[i] = live ? buf[4 + q][i] : 0.0f;
+        finish(b, live, u, wn);
     }
-    for (int r = ACT_ROUNDS; r < rounds; r++) {
+#pragma unroll 1
+    for (int r = XR; r < rounds; r++) {
         const int b0 = (r * nwarps + warp) * 4;
         if (b0 >= nb)
             break; // warp-uniform
@@ -769,16 +803,17 @@ __device__ __forceinline__ bool gemv_produce(const CUtensorMap *tw, const CUtens
 // across ops; advanced to the op's end on return).  dep_wait: the prologue
 // waits for the previous kernel itself (after the loads that do not depend on
 // it); otherwise the caller has already waited for the op's input.
-template <int WF, int ST, int PRO, int EPI>
-__device__ __forceinline__ void gemv_consume(const GemvParams &p, const GemvWork &w, const GemvSmem &sm, uint32_t &cpar,
-                             uint32_t &lpar, int ctid, bool dep_wait = false)
+template <int WF, int ST>
+__device__ __forceinline__ void gemv_consume(const GemvParams &p, const int pro, const int epi, const GemvWork &w,
+                                             const GemvSmem &sm, uint32_t &cpar, uint32_t &lpar, int ctid,
+                                             bool dep_wait = false)
 {
     constexpr int W_ROW = CB * wbytes_per_block(WF);
     constexpr int S_ROW = CB * sbytes(ST);
     const int warp = ctid >> 5, lane = ctid & 31;
     const int SPG = sm.S / NG;
     LLMRS_TRACE_BEGIN(2);
-    load_activation<WF, PRO>(p, sm.act, sm.act_s, sm.act_c, sm.red, ctid, PRO_THREADS, 1, sm.issued, dep_wait);
+    load_activation<WF>(p, pro, sm.act, sm.act_s, sm.act_c, sm.red, ctid, PRO_THREADS, 1, sm.issued, dep_wait);
     named_bar_sync(1, PRO_THREADS);
     if (ctid == 0) {
         trace_ready(p.trace, p.trace_slot);
@@ -796,10 +831,9 @@ __device__ __forceinline__ void gemv_consume(const GemvParams &p, const GemvWork
     unsigned long long best = 0ull;
     bool ok = true;
     uint32_t mypar = cpar; // this group's stages flip as it consumes them
-    // the step loop, specialised for the number of groups per tile set
-    auto steps = [&](auto gt_tag) {
-        constexpr int GT = decltype(gt_tag)::value;
-        constexpr int TPS = NG / GT;
+    // the step loop (one copy for every number of groups per tile set)
+    {
+        const int GT = w.GT, TPS = w.TPS;
         float acc = 0.0f; // running sum of row ri (complete in the segment-3 lanes)
         const int tset = grp % TPS, q = grp / TPS;
         const int prevw = (tset + TPS * ((q + GT - 1) % GT)) * WPG + wq; // previous step's warp
@@ -908,42 +942,36 @@ __device__ __forceinline__ void gemv_consume(const GemvParams &p, const GemvWork
                 // ---- epilogue: lanes of segment 3 hold the complete rows
                 const int row = trow0 + wq * RPW + ri;
                 const bool valid = seg == 3 && live_row;
-                if (EPI == EPI_STORE) {
+                if (epi == EPI_STORE) {
                     if (valid)
                         p.y[row] = acc;
-                } else if (EPI == EPI_RESIDUAL) {
+                } else if (epi == EPI_RESIDUAL) {
                     if (valid)
                         p.y[row] = __fadd_rn(acc, __ldcg(p.residual + row));
-                } else if (EPI == EPI_SILU) {
+                } else if (epi == EPI_SILU) {
                     const float up = __shfl_down_sync(0xffffffffu, acc, 1);
                     if (valid && (row & 1) == 0) {
                         const float silu = __fdiv_rn(acc, __fadd_rn(1.0f, expf(-acc)));
                         p.y[row >> 1] = __fmul_rn(silu, up);
                     }
-                } else if (EPI == EPI_ARGMAX) {
+                } else if (epi == EPI_ARGMAX) {
                     if (valid) {
                         if (p.y)
                             p.y[row] = acc;
                         const unsigned long long key = argmax_key(acc, (uint32_t)(row + p.row_offset));
                         best = key > best ? key : best;
                     }
-                } else if (EPI == EPI_PARTIAL) {
+                } else if (epi == EPI_PARTIAL) {
                     if (valid)
                         partial_store(p, row, acc);
                 }
             }
         }
-    };
-    if (w.GT == 1)
-        steps(std::integral_constant<int, 1>{});
-    else if (w.GT == 2)
-        steps(std::integral_constant<int, 2>{});
-    else
-        steps(std::integral_constant<int, 4>{});
+    }
     // every consumer thread advances the op-start parities identically
     cpar ^= gemv_stage_use_parity(w, sm.S);
     lpar ^= gemv_link_parity(w);
-    if (EPI == EPI_ARGMAX)
+    if (epi == EPI_ARGMAX)
         argmax_finalize(p, best, ctid, PRO_THREADS, 1);
 }
 

@@ -792,7 +792,7 @@ __global__ void __launch_bounds__(PG_QUANT_THREADS) prefill_quant_kernel(const P
     p.eps = a.eps;
     p.K = K;
     p.err = a.err;
-    load_activation<WF, PRO>(p, act, act_s, act_c, red, threadIdx.x, PG_QUANT_THREADS, 1, nullptr);
+    load_activation<WF>(p, PRO, act, act_s, act_c, red, threadIdx.x, PG_QUANT_THREADS, 1, nullptr);
     __syncthreads();
     if (BF) { // codes as bf16 (exact: |code| <= 127), 8 per 16-byte store
         uint4 *dst = reinterpret_cast<uint4 *>(reinterpret_cast<__nv_bfloat16 *>(a.q) + (size_t)m * K);
