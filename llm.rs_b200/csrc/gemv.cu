@@ -68,11 +68,15 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     sm.act_s = reinterpret_cast<float *>(smem + L.acts_off);
     sm.act_c = reinterpret_cast<int *>(smem + L.actc_off);
     sm.tbuf = reinterpret_cast<float *>(smem + L.tb_off);
+    sm.prod = sm.tbuf; // a CTA uses the transpose buffers or the product slots, never both
     sm.linkbuf = reinterpret_cast<float *>(smem + L.link_off);
     sm.full = reinterpret_cast<uint64_t *>(smem + L.bar_off);
     sm.empty = sm.full + S;
     sm.link = sm.empty + S;
     sm.issued = sm.link + NW;
+    sm.pfull = sm.issued + 1;
+    sm.pempty = sm.pfull + PSLOTS;
+    sm.sbest = reinterpret_cast<unsigned long long *>(sm.pempty + PSLOTS);
     sm.red = reinterpret_cast<float *>(smem + L.red_off);
     const GemvWork w = gemv_work(p, blockIdx.x);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -85,12 +89,21 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         for (int i = 0; i < NW; i++)
             mbar_init(&sm.link[i], 1);
         mbar_init(sm.issued, NW);
+        for (int i = 0; i < PSLOTS; i++) {
+            mbar_init(&sm.pfull[i], WPG); // written by the 4 warps of a group
+            mbar_init(&sm.pempty[i], 1);  // released by a summer warp
+        }
+        *sm.sbest = 0ull;
         fence_mbar_init();
         trace_start(p.trace, p.trace_slot);
     }
     __syncthreads();
 
-    if (warp == NW) {
+    if (warp >= NW && warp < NW + NSUM) { // summer warps (used when groups share a tile)
+        gemv_sum(p, p.epi, w, sm, warp - NW);
+        return;
+    }
+    if (warp == NW + NSUM) {
         // Weights do not depend on the previous kernel: the first n_pre stages
         // stream right away, the rest once the consumers have requested the
         // activation (queued behind the weight stream it would arrive last).

@@ -29,11 +29,13 @@ constexpr int NG = 4;                    // consumer warp groups (one pipeline s
 constexpr int WPG = 4;                   // warps per group
 constexpr int RPW = 8;                   // tile rows per warp (WPG * RPW = 32)
 constexpr int NW = NG * WPG;             // consumer warps
-constexpr int NTHREADS = (NW + 1) * 32;  // + producer warp
+constexpr int NSUM = 2;                  // summer warps: in-order row sums when groups share a tile
+constexpr int NTHREADS = (NW + NSUM + 1) * 32; // + summers + producer warp
 constexpr int TR = 32;                   // max rows per tile
 constexpr int CB = 32;                   // blocks per chunk (1024 weights), one per lane
 constexpr int TBS = 36;                  // transpose row stride (floats): 16-byte aligned, conflict-free
-constexpr size_t SMEM_BUDGET = 200 * 1024; // one CTA per SM (544 threads): use most of the SM's shared memory
+constexpr int PSLOTS = 8;                // product slots [TR rows][TBS] shared by the tile sets of a CTA
+constexpr size_t SMEM_BUDGET = 224 * 1024; // one CTA per SM: use most of the SM's shared memory
 constexpr int MAX_STAGES = 8;
 constexpr int PRO_THREADS = NW * 32;
 
@@ -44,6 +46,14 @@ __host__ __device__ constexpr size_t align_up(size_t x, size_t a) { return (x + 
 struct SmemLayout {
     size_t stage_bytes, scale_off, act_off, acts_off, actc_off, tb_off, link_off, bar_off, red_off, total;
 };
+
+// bytes of the region that holds either the per-warp transpose buffers (one
+// group per tile) or the product slots (groups sharing a tile): a CTA uses one
+__host__ __device__ constexpr size_t tb_region_bytes()
+{
+    return (size_t)NW * RPW * TBS * 4 > (size_t)PSLOTS * TR * TBS * 4 ? (size_t)NW * RPW * TBS * 4
+                                                                     : (size_t)PSLOTS * TR * TBS * 4;
+}
 
 // offsets are relative to a 128-byte aligned base
 __host__ __device__ inline SmemLayout smem_layout(int wf, int st, int K, int stages)
@@ -56,9 +66,10 @@ __host__ __device__ inline SmemLayout smem_layout(int wf, int st, int K, int sta
     L.acts_off = L.act_off + (size_t)nb * 32;
     L.actc_off = align_up(L.acts_off + (size_t)nb * 4, 16);
     L.tb_off = align_up(L.actc_off + (size_t)nb * 4, 16);
-    L.link_off = L.tb_off + (size_t)NW * RPW * TBS * 4;
+    L.link_off = L.tb_off + tb_region_bytes();
     L.bar_off = align_up(L.link_off + (size_t)NW * RPW * 4, 16);
-    L.red_off = L.bar_off + (size_t)(2 * stages + NW + 1) * 8; // full, empty, link, activation-issued
+    // full, empty, link, activation-issued, product full / empty, summers' argmax key
+    L.red_off = L.bar_off + (size_t)(2 * stages + NW + 1 + 2 * PSLOTS + 1) * 8;
     L.total = align_up(L.red_off + 16 * 4, 16) + 128; // + slack to align the base
     return L;
 }
@@ -629,10 +640,13 @@ struct GemvSmem {
     uint64_t *full, *empty;  // [S] each: filled by the producer / released by a warp group
     uint64_t *link;          // [NW]: running-sum handoff between groups
     uint64_t *issued;        // activation requested (one-kernel path only; nullptr otherwise)
+    uint64_t *pfull, *pempty; // [PSLOTS]: product slot written by a group / summed by a summer
+    unsigned long long *sbest; // summers' best argmax key
     uint32_t *act;           // quantised activation, packed per block
     float *act_s;            // activation block scales
     int *act_c;              // per block: -8 * sum(q) (Q4 offset)
     float *tbuf, *linkbuf, *red;
+    float *prod;             // [PSLOTS][TR][TBS] block products (aliases tbuf: a CTA uses one)
     unsigned long long *ready_mark = nullptr; // optional: latest time a CTA finished the prologue
 };
 
@@ -797,6 +811,36 @@ __device__ __forceinline__ bool gemv_produce(const CUtensorMap *tw, const CUtens
     return true;
 }
 
+// Output of one finished row (valid: this lane holds a row of the tile).
+// Every lane of the warp calls it (the SiLU pair crosses lanes).
+__device__ __forceinline__ void gemv_epilogue(const GemvParams &p, const int epi, int row, bool valid, float acc,
+                                              unsigned long long &best)
+{
+    if (epi == EPI_STORE) {
+        if (valid)
+            p.y[row] = acc;
+    } else if (epi == EPI_RESIDUAL) {
+        if (valid)
+            p.y[row] = __fadd_rn(acc, __ldcg(p.residual + row));
+    } else if (epi == EPI_SILU) {
+        const float up = __shfl_down_sync(0xffffffffu, acc, 1);
+        if (valid && (row & 1) == 0) {
+            const float silu = __fdiv_rn(acc, __fadd_rn(1.0f, expf(-acc)));
+            p.y[row >> 1] = __fmul_rn(silu, up);
+        }
+    } else if (epi == EPI_ARGMAX) {
+        if (valid) {
+            if (p.y)
+                p.y[row] = acc;
+            const unsigned long long key = argmax_key(acc, (uint32_t)(row + p.row_offset));
+            best = key > best ? key : best;
+        }
+    } else if (epi == EPI_PARTIAL) {
+        if (valid)
+            partial_store(p, row, acc);
+    }
+}
+
 // Consumers (the NW consumer warps, ctid = 0 .. NW*32-1): prologue, steps,
 // epilogue of one GEMV.  cpar / lpar: per stage, parity of the full-barrier
 // phase to wait for next; per warp, parity of its link arrivals so far (kept
@@ -836,8 +880,6 @@ __device__ __forceinline__ void gemv_consume(const GemvParams &p, const int pro,
         const int GT = w.GT, TPS = w.TPS;
         float acc = 0.0f; // running sum of row ri (complete in the segment-3 lanes)
         const int tset = grp % TPS, q = grp / TPS;
-        const int prevw = (tset + TPS * ((q + GT - 1) % GT)) * WPG + wq; // previous step's warp
-        const uint32_t link0 = (lpar >> prevw) & 1u;                   // its arrivals before this op
         const int my_iters = gemv_group_iters(w, grp);
         int c = q, tile = tset; // this group's first step u = q
         while (c >= w.nchunks) {
@@ -892,6 +934,23 @@ __device__ __forceinline__ void gemv_consume(const GemvParams &p, const int pro,
             __syncwarp();
             if (lane == 0)
                 mbar_arrive(&sm.empty[s]);
+            if (GT > 1) {
+                // groups share the tile: the products go to the set's slot for
+                // step u, and the set's summer warp adds them in block order
+                const int ps = PSLOTS / TPS;
+                const int slot = tset * ps + u % ps, use = u / ps;
+                if (use > 0 && ok && !mbar_wait(&sm.pempty[slot], (uint32_t)((use - 1) & 1), p.err))
+                    ok = false;
+                float *P = sm.prod + (size_t)slot * TR * TBS + (size_t)(wq * RPW) * TBS + lane;
+#pragma unroll
+                for (int i = 0; i < RPW; i++)
+                    P[i * TBS] = t[i];
+                __syncwarp();
+                if (lane == 0)
+                    mbar_arrive(&sm.pfull[slot]);
+                LLMRS_TRACE_END(4);
+                continue;
+            }
             // transpose: lane j then holds row ri's products for blocks seg*8 .. +7
 #pragma unroll
             for (int i = 0; i < RPW; i++)
@@ -900,18 +959,9 @@ __device__ __forceinline__ void gemv_consume(const GemvParams &p, const int pro,
             const float4 v0 = *reinterpret_cast<const float4 *>(tb + ri * TBS + seg * 8);
             const float4 v1 = *reinterpret_cast<const float4 *>(tb + ri * TBS + seg * 8 + 4);
             const float v[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
-            if (GT == 1) { // the running sum moves from the segment-3 lane to the segment-0 lane
+            { // the running sum moves from the segment-3 lane to the segment-0 lane
                 const float carry = __shfl_sync(0xffffffffu, acc, 3 * RPW + ri);
                 acc = (c > 0 && seg == 0) ? carry : 0.0f;
-            } else { // ... or arrives from the previous step's warp
-                acc = 0.0f;
-                if (u > 0) {
-                    const int kp = q > 0 ? k : k - 1; // that warp's step index
-                    if (ok && !mbar_wait(&sm.link[prevw], link0 ^ (uint32_t)(kp & 1), p.err))
-                        ok = false;
-                    if (c > 0 && seg == 0)
-                        acc = sm.linkbuf[prevw * RPW + ri];
-                }
             }
             // add the chunk's blocks in order: segment 0 first, then 1, 2, 3
             const bool live_row = wq * RPW + ri < rows;
@@ -929,50 +979,83 @@ __device__ __forceinline__ void gemv_consume(const GemvParams &p, const int pro,
                             acc = __fadd_rn(acc, v[kk]);
                 }
             }
-            if (GT > 1) {
-                __syncwarp();
-                if (seg == 3)
-                    sm.linkbuf[warp * RPW + ri] = acc;
-                __syncwarp();
-                if (lane == 0)
-                    mbar_arrive(&sm.link[warp]);
-            }
             LLMRS_TRACE_END(4);
-            if (c == w.nchunks - 1) {
-                // ---- epilogue: lanes of segment 3 hold the complete rows
-                const int row = trow0 + wq * RPW + ri;
-                const bool valid = seg == 3 && live_row;
-                if (epi == EPI_STORE) {
-                    if (valid)
-                        p.y[row] = acc;
-                } else if (epi == EPI_RESIDUAL) {
-                    if (valid)
-                        p.y[row] = __fadd_rn(acc, __ldcg(p.residual + row));
-                } else if (epi == EPI_SILU) {
-                    const float up = __shfl_down_sync(0xffffffffu, acc, 1);
-                    if (valid && (row & 1) == 0) {
-                        const float silu = __fdiv_rn(acc, __fadd_rn(1.0f, expf(-acc)));
-                        p.y[row >> 1] = __fmul_rn(silu, up);
-                    }
-                } else if (epi == EPI_ARGMAX) {
-                    if (valid) {
-                        if (p.y)
-                            p.y[row] = acc;
-                        const unsigned long long key = argmax_key(acc, (uint32_t)(row + p.row_offset));
-                        best = key > best ? key : best;
-                    }
-                } else if (epi == EPI_PARTIAL) {
-                    if (valid)
-                        partial_store(p, row, acc);
-                }
-            }
+            if (c == w.nchunks - 1) // epilogue: lanes of segment 3 hold the complete rows
+                gemv_epilogue(p, epi, trow0 + wq * RPW + ri, seg == 3 && live_row, acc, best);
         }
     }
     // every consumer thread advances the op-start parities identically
     cpar ^= gemv_stage_use_parity(w, sm.S);
     lpar ^= gemv_link_parity(w);
-    if (epi == EPI_ARGMAX)
+    if (epi == EPI_ARGMAX) {
+        // rows summed by the summer warps (groups sharing a tile) add their key
+        named_bar_sync(2, PRO_THREADS + NSUM * 32);
+        const unsigned long long sb = *reinterpret_cast<volatile unsigned long long *>(sm.sbest);
+        best = sb > best ? sb : best;
         argmax_finalize(p, best, ctid, PRO_THREADS, 1);
+    }
+}
+
+// Summer warp `tset` of a CTA whose groups share tiles (GT > 1): lane r adds
+// row r's block products of every step of tile set tset in block order (the
+// reference's sequential sum), releases each product slot as soon as its
+// values are in registers, and runs the epilogue of the tile's rows.
+__device__ __forceinline__ void gemv_sum(const GemvParams &p, const int epi, const GemvWork &w, const GemvSmem &sm,
+                                         int tset)
+{
+    const int lane = threadIdx.x & 31;
+    unsigned long long best = 0ull;
+    if (w.GT > 1 && tset < w.TPS) {
+        const int TPS = w.TPS, ps = PSLOTS / TPS;
+        const int nset = w.ntiles > tset ? (w.ntiles - 1 - tset) / TPS + 1 : 0;
+        const int U = nset * w.nchunks;
+        float acc = 0.0f;
+        int c = 0, tile = tset;
+        bool ok = true;
+        for (int u = 0; u < U; u++) {
+            const int slot = tset * ps + u % ps;
+            if (ok && !mbar_wait(&sm.pfull[slot], (uint32_t)((u / ps) & 1), p.err))
+                ok = false;
+            const float4 *P = reinterpret_cast<const float4 *>(sm.prod + (size_t)slot * TR * TBS + (size_t)lane * TBS);
+            float v[CB];
+#pragma unroll
+            for (int j = 0; j < CB / 4; j++) {
+                const float4 f = P[j];
+                v[4 * j] = f.x;
+                v[4 * j + 1] = f.y;
+                v[4 * j + 2] = f.z;
+                v[4 * j + 3] = f.w;
+            }
+            __syncwarp();
+            if (lane == 0)
+                mbar_arrive(&sm.pempty[slot]);
+            const int nbc = min(CB, w.nb - c * CB);
+            if (c == 0)
+                acc = 0.0f;
+#pragma unroll
+            for (int kk = 0; kk < CB; kk++)
+                if (kk < nbc)
+                    acc = __fadd_rn(acc, v[kk]);
+            if (c == w.nchunks - 1) {
+                const int trow0 = w.r0 + tile * w.B;
+                gemv_epilogue(p, epi, trow0 + lane, lane < min(w.B, w.r1 - trow0), acc, best);
+            }
+            if (++c == w.nchunks) {
+                c = 0;
+                tile += TPS;
+            }
+        }
+    }
+    if (epi == EPI_ARGMAX) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+            best = other > best ? other : best;
+        }
+        if (lane == 0 && best)
+            atomicMax(sm.sbest, best);
+        named_bar_sync(2, PRO_THREADS + NSUM * 32);
+    }
 }
 
 } // namespace
