@@ -683,3 +683,25 @@ def connect_tensor_parallel(model, group=None):
     dist.all_gather_object(handles, handle, group=group)
     model.tp_connect(handles)
     dist.barrier(group)
+
+
+def tp_sample(model, recent, repeat_penalty, temperature, top_p, u, group=None):
+    """Next-token sampling (src/main.rs:192-305) for a tensor-parallel model.
+
+    Each rank holds the last step's logits for its vocabulary rows
+    [rank*V/T, (rank+1)*V/T).  The shards are gathered over the host channel
+    (torch.distributed, any backend), and every rank runs the device sampler
+    (llmrs_sample) over the full vocabulary on its own GPU with the same draw
+    `u`, so all ranks pick the same token.  Every rank calls this in the same
+    order with the same arguments."""
+    import torch
+    import torch.distributed as dist
+
+    shard = torch.from_numpy(model.logits())
+    parts = [torch.empty_like(shard) for _ in range(dist.get_world_size(group))]
+    dist.all_gather(parts, shard, group=group)
+    full = DeviceTensor.from_numpy(model.ctx, torch.cat(parts).numpy())
+    try:
+        return CudaBackend(model.ctx).sample(full, recent, repeat_penalty, temperature, top_p, u)
+    finally:
+        full.free()

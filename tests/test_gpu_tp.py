@@ -121,3 +121,24 @@ def test_tensor_parallel_decode_matches_oracle(orc, world, shape):
         tol = LOGIT_ABS * max(1.0, float(np.abs(o).max()) / LOGIT_SCALE_REF)
         rel = float(np.linalg.norm((gl - o).astype(np.float64)) / np.linalg.norm(o.astype(np.float64)))
         assert float(np.abs(gl - o).max()) < tol and rel < LOGIT_REL_L2, (step, float(np.abs(gl - o).max()), rel)
+
+
+def test_tensor_parallel_sampling_matches_oracle(orc):
+    """Sampling (src/main.rs:192-305) on a 2-rank model: the vocabulary shards
+    of the last step's logits are gathered and every rank samples the full
+    distribution with the same draw; all ranks pick the oracle's token."""
+    world = 2
+    if n_gpus() < world:
+        pytest.skip("needs %d GPUs" % world)
+    cfg = dict(n_layers=2, hidden=512, n_heads=8, n_kv_heads=2, head_dim=64, ffn=1024, vocab=1000,
+               max_seq=96, rms_eps=1e-5, rope_theta=500000.0, weight_format=0, tied_embeddings=1, scale_dtype=0)
+    prompt, recent = [5, 17, 900, 3], [5, 17, 900, 3, 3]
+    settings = [(1.2, 0.8, 0.9, 0.1), (1.0, 1.0, 1.0, 0.5), (1.3, 0.7, 0.95, 0.93)]
+    got = run_tp(world, dict(cfg=cfg, seed=21, prompt=prompt, forced=[], kv=0, sample=settings, recent=recent))
+    logits = np.asarray(got[0]["logits"], np.float32)        # rank shards in rank order: the full vocabulary
+    samples = got[-1]["samples"]
+    for i, (penalty, temperature, top_p, u) in enumerate(settings):
+        toks = [samples[r][i] for r in range(world)]
+        assert len(set(toks)) == 1, toks                       # every rank picks the same token
+        t_orc, margin = orc.sample(logits, recent, penalty, temperature, top_p, u)
+        assert toks[0] == t_orc or margin < 1e-6, (i, toks, t_orc, margin)

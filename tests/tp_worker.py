@@ -51,14 +51,21 @@ def main():
         tok, lg = m.decode_step(t, pos)
         steps.append((tok, lg))
         pos += 1
+    samples = []
+    for (penalty, temperature, top_p, u) in spec.get("sample", []):  # after the last step, same draw on every rank
+        samples.append(L.tp_sample(m, spec["recent"], penalty, temperature, top_p, u))
     got = [None] * world
     dist.all_gather_object(got, [(int(t), l.astype(np.float32).tobytes()) for t, l in steps])
+    sampled = [None] * world
+    dist.all_gather_object(sampled, samples)
     if rank == 0:
         out = []
         for i in range(len(steps)):
             toks = [got[r][i][0] for r in range(world)]
             logits = np.concatenate([np.frombuffer(got[r][i][1], np.float32) for r in range(world)])
             out.append({"tokens": toks, "logits": logits.tolist()})
+        if spec.get("sample"):
+            out.append({"samples": sampled})
         print("TPRESULT " + json.dumps(out))
     dist.barrier()
     m.close()
