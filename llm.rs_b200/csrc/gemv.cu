@@ -47,7 +47,7 @@ namespace {
 // run-time choices (p.pro, p.epi), so the five GEMVs of a decode layer run the
 // same code and keep it in the SM's instruction cache from launch to launch
 // (one instantiation per variant made every launch refetch its code).
-template <int WF, int ST>
+template <int WF, int ST, bool TPK>
 __global__ void __launch_bounds__(NTHREADS, 1)
     gemv_tma_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap ts, const GemvParams p)
 {
@@ -117,7 +117,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
     const int ctid = threadIdx.x;
     uint32_t cpar = 0, lpar = 0;
-    gemv_consume<WF, ST>(p, p.pro, p.epi, w, sm, cpar, lpar, ctid, true); // waits for the previous kernel itself
+    gemv_consume<WF, ST, TPK>(p, p.pro, p.epi, w, sm, cpar, lpar, ctid, true); // waits for the previous kernel itself
     LLMRS_TRACE_FLUSH(0);
     if (ctid == 0)
         trace_end(p.trace, p.trace_slot);
@@ -138,7 +138,7 @@ __global__ void __launch_bounds__(SIMPLE_THREADS) gemv_simple_kernel(const GemvP
     int *act_c = reinterpret_cast<int *>(act_s + nb);
     float *red = reinterpret_cast<float *>(act_c + nb);
     griddep_wait();
-    load_activation<WF>(p, PRO, act, act_s, act_c, red, threadIdx.x, SIMPLE_THREADS, 1, nullptr);
+    load_activation<WF, PRO == PRO_AR_NORM>(p, PRO, act, act_s, act_c, red, threadIdx.x, SIMPLE_THREADS, 1, nullptr);
     named_bar_sync(1, SIMPLE_THREADS);
     const int row = blockIdx.x * blockDim.x + threadIdx.x;
     unsigned long long best = 0ull;
@@ -224,8 +224,12 @@ constexpr int SIMPLE_SMEM_MAX = 200 * 1024;
 template <int WF, int ST>
 cudaError_t prepare_fast()
 {
-    return cudaFuncSetAttribute(gemv_tma_kernel<WF, ST>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                (int)SMEM_BUDGET + 2048);
+    cudaError_t e = cudaFuncSetAttribute(gemv_tma_kernel<WF, ST, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)SMEM_BUDGET + 2048);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(gemv_tma_kernel<WF, ST, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)SMEM_BUDGET + 2048);
+    return e;
 }
 
 template <int WF, int ST, int PRO, int EPI>
@@ -245,8 +249,14 @@ int launch_fast(const GemvPlan &plan, const GemvParams &p0, int pro, int epi, cu
     p.n_pre = gemv_prefetch_stages();
     p.box_rows = plan.box_rows;
     p.rows_per_cta = plan.rows_per_cta;
-    LLMRS_CUDA_TRY(launch(gemv_tma_kernel<WF, ST>, dim3(plan.grid), dim3(NTHREADS), plan.smem, stream, pdl, plan.tw,
-                          plan.ts, p));
+    // tensor-parallel launches (every GEMV of a tensor-parallel step) share the
+    // instantiation that holds the peer-polling prologue
+    if (p.tp)
+        LLMRS_CUDA_TRY(launch(gemv_tma_kernel<WF, ST, true>, dim3(plan.grid), dim3(NTHREADS), plan.smem, stream, pdl,
+                              plan.tw, plan.ts, p));
+    else
+        LLMRS_CUDA_TRY(launch(gemv_tma_kernel<WF, ST, false>, dim3(plan.grid), dim3(NTHREADS), plan.smem, stream, pdl,
+                              plan.tw, plan.ts, p));
     return LLMRS_OK;
 }
 

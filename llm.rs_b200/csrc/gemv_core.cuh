@@ -266,20 +266,86 @@ __device__ __forceinline__ void st_volatile_u64(unsigned long long *a, unsigned 
     asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(a), "l"(v) : "memory");
 }
 
+// Tensor parallel: the sum, in rank order, of the ranks' 4 partial values at
+// `off` of this rank's receive buffer ([nparts][stride] tagged 64-bit words),
+// once every word carries `tag`.  Ranks go in groups of 2: a group's words are
+// requested at once and only those still without the tag are polled again, so
+// the wait costs about one memory round trip per group, not one per rank.
+// Gives up after peer_ns (zeros, DEV_ERR_PEER_TIMEOUT).
+__device__ __forceinline__ void ar_gather4(const unsigned long long *part, size_t stride, int nparts, size_t off,
+                                        uint32_t tag, uint64_t peer_ns, uint32_t *err, float (&s)[4])
+{
+    constexpr int ARG = 2; // ranks per group
+    s[0] = s[1] = s[2] = s[3] = 0.0f;
+    for (int q0 = 0; q0 < nparts; q0 += ARG) {
+        ulonglong2 wa[ARG], wc[ARG];
+#pragma unroll
+        for (int g = 0; g < ARG; g++) {
+            const unsigned long long *src = part + (size_t)min(q0 + g, nparts - 1) * stride + off;
+            wa[g] = ld_volatile_u64x2(src);
+            wc[g] = ld_volatile_u64x2(src + 2);
+        }
+        auto arrived = [&](int g) {
+            return (uint32_t)(wa[g].x >> 32) == tag && (uint32_t)(wa[g].y >> 32) == tag &&
+                   (uint32_t)(wc[g].x >> 32) == tag && (uint32_t)(wc[g].y >> 32) == tag;
+        };
+        uint64_t t0 = 0;
+        for (uint32_t spin = 0;; spin++) {
+            bool all = true;
+#pragma unroll
+            for (int g = 0; g < ARG; g++)
+                all = all && arrived(g);
+            if (all)
+                break;
+#pragma unroll
+            for (int g = 0; g < ARG; g++)
+                if (!arrived(g)) {
+                    const unsigned long long *src = part + (size_t)min(q0 + g, nparts - 1) * stride + off;
+                    wa[g] = ld_volatile_u64x2(src);
+                    wc[g] = ld_volatile_u64x2(src + 2);
+                }
+            if ((spin & 63u) == 0u) {
+                const uint64_t now = globaltimer_ns();
+                if (spin == 0u)
+                    t0 = now;
+                else if (now - t0 > peer_ns || *reinterpret_cast<volatile uint32_t *>(err) == DEV_ERR_PEER_TIMEOUT) {
+                    atomicCAS(err, 0u, (uint32_t)DEV_ERR_PEER_TIMEOUT);
+#pragma unroll
+                    for (int g = 0; g < ARG; g++)
+                        wa[g] = wc[g] = make_ulonglong2(0ull, 0ull);
+                    break;
+                }
+            }
+        }
+#pragma unroll
+        for (int g = 0; g < ARG; g++) {
+            if (q0 + g >= nparts)
+                break;
+            const float w[4] = {__uint_as_float((uint32_t)wa[g].x), __uint_as_float((uint32_t)wa[g].y),
+                                __uint_as_float((uint32_t)wc[g].x), __uint_as_float((uint32_t)wc[g].y)};
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+                s[i] = (q0 + g == 0) ? w[i] : __fadd_rn(s[i], w[i]);
+        }
+    }
+}
+
 // dep_wait: this thread has not yet waited for the previous kernel; the loads
 // that do not depend on it (RMSNorm weights) are issued first, then the wait.
 // `pro` is a GemvPro: a run-time value in the decode kernel (one binary serves
 // every prologue, so the step's kernels share their code in the instruction
 // cache), a constant where a caller inlines it for one prologue.
-template <int WF>
+template <int WF, bool TPK = false>
 __device__ __forceinline__ void load_activation(const GemvParams &p, const int pro, uint32_t *act, float *act_s,
                                                 int *act_c, float *red, int tid, int nthr, int bar, uint64_t *issued,
                                                 bool dep_wait = false)
 {
     const int K = p.K, nb = K >> 5;
     const bool has = tid < nb;
-    const bool NORM = pro == PRO_NORM || pro == PRO_EMBED_NORM || pro == PRO_AR_NORM;
-    const bool AR = pro == PRO_AR_NORM;
+    // TPK: this instantiation serves tensor-parallel launches (the peer-polling
+    // prologue is compiled only there, out of the single-GPU kernel)
+    const bool NORM = pro == PRO_NORM || pro == PRO_EMBED_NORM || (TPK && pro == PRO_AR_NORM);
+    const bool AR = TPK && pro == PRO_AR_NORM;
     const bool EARLY_W = pro == PRO_NORM || pro == PRO_EMBED_NORM; // norm weights loaded before the wait
     if (!EARLY_W && dep_wait) {
         griddep_wait();
@@ -335,36 +401,10 @@ __device__ __forceinline__ void load_activation(const GemvParams &p, const int p
         nparts = tp->size;
         tag = ar_tag(p);
     }
-    // AR: the 4 partial values of rank q at off, once every word carries this
-    // exchange's tag (each 8-byte word is written whole, so a matching tag
-    // means its value is the one sent); gives up after p.peer_ns (default 5 s)
+    // AR: a rank's 8-byte words carry this exchange's tag (each word is
+    // written whole, so a matching tag means its value is the one sent); the
+    // wait gives up after p.peer_ns (default 5 s)
     const uint64_t peer_ns = p.peer_ns ? p.peer_ns : 5000000000ull;
-    auto ll_load4 = [&](int q, size_t off, float (&v)[4]) {
-        const unsigned long long *src = part + (size_t)q * K + off;
-        uint64_t t0 = 0;
-        for (uint32_t spin = 0;; spin++) {
-            const ulonglong2 a = ld_volatile_u64x2(src), c = ld_volatile_u64x2(src + 2);
-            if ((uint32_t)(a.x >> 32) == tag && (uint32_t)(a.y >> 32) == tag && (uint32_t)(c.x >> 32) == tag &&
-                (uint32_t)(c.y >> 32) == tag) {
-                v[0] = __uint_as_float((uint32_t)a.x);
-                v[1] = __uint_as_float((uint32_t)a.y);
-                v[2] = __uint_as_float((uint32_t)c.x);
-                v[3] = __uint_as_float((uint32_t)c.y);
-                return;
-            }
-            if ((spin & 63u) == 0u) {
-                const uint64_t now = globaltimer_ns();
-                if (spin == 0u)
-                    t0 = now;
-                else if (now - t0 > peer_ns ||
-                         *reinterpret_cast<volatile uint32_t *>(p.err) == DEV_ERR_PEER_TIMEOUT) {
-                    atomicCAS(p.err, 0u, (uint32_t)DEV_ERR_PEER_TIMEOUT);
-                    v[0] = v[1] = v[2] = v[3] = 0.0f;
-                    return;
-                }
-            }
-        }
-    };
     // the 4 values of block b this lane holds: x, or (AR) the ranks' partial
     // sums in rank order, then + x
     auto load4 = [&](int b, float (&u)[4]) {
@@ -375,14 +415,8 @@ __device__ __forceinline__ void load_activation(const GemvParams &p, const int p
         u[2] = t.z;
         u[3] = t.w;
         if (AR) {
-            float s[4], w[4];
-            ll_load4(0, off, s);
-            for (int q = 1; q < nparts; q++) {
-                ll_load4(q, off, w);
-#pragma unroll
-                for (int i = 0; i < 4; i++)
-                    s[i] = __fadd_rn(s[i], w[i]);
-            }
+            float s[4];
+            ar_gather4(part, (size_t)K, nparts, off, tag, peer_ns, p.err, s);
 #pragma unroll
             for (int i = 0; i < 4; i++)
                 u[i] = __fadd_rn(s[i], u[i]);
@@ -847,7 +881,7 @@ __device__ __forceinline__ void gemv_epilogue(const GemvParams &p, const int epi
 // across ops; advanced to the op's end on return).  dep_wait: the prologue
 // waits for the previous kernel itself (after the loads that do not depend on
 // it); otherwise the caller has already waited for the op's input.
-template <int WF, int ST>
+template <int WF, int ST, bool TPK = false>
 __device__ __forceinline__ void gemv_consume(const GemvParams &p, const int pro, const int epi, const GemvWork &w,
                                              const GemvSmem &sm, uint32_t &cpar, uint32_t &lpar, int ctid,
                                              bool dep_wait = false)
@@ -857,7 +891,7 @@ __device__ __forceinline__ void gemv_consume(const GemvParams &p, const int pro,
     const int warp = ctid >> 5, lane = ctid & 31;
     const int SPG = sm.S / NG;
     LLMRS_TRACE_BEGIN(2);
-    load_activation<WF>(p, pro, sm.act, sm.act_s, sm.act_c, sm.red, ctid, PRO_THREADS, 1, sm.issued, dep_wait);
+    load_activation<WF, TPK>(p, pro, sm.act, sm.act_s, sm.act_c, sm.red, ctid, PRO_THREADS, 1, sm.issued, dep_wait);
     named_bar_sync(1, PRO_THREADS);
     if (ctid == 0) {
         trace_ready(p.trace, p.trace_slot);
