@@ -69,11 +69,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     sm.act_c = reinterpret_cast<int *>(smem + L.actc_off);
     sm.tbuf = reinterpret_cast<float *>(smem + L.tb_off);
     sm.prod = sm.tbuf; // a CTA uses the transpose buffers or the product slots, never both
-    sm.linkbuf = reinterpret_cast<float *>(smem + L.link_off);
     sm.full = reinterpret_cast<uint64_t *>(smem + L.bar_off);
     sm.empty = sm.full + S;
-    sm.link = sm.empty + S;
-    sm.issued = sm.link + NW;
+    sm.issued = sm.empty + S;
     sm.pfull = sm.issued + 1;
     sm.pempty = sm.pfull + PSLOTS;
     sm.sbest = reinterpret_cast<unsigned long long *>(sm.pempty + PSLOTS);
@@ -86,8 +84,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             mbar_init(&sm.full[s], 1);
             mbar_init(&sm.empty[s], WPG); // released by the group's warps
         }
-        for (int i = 0; i < NW; i++)
-            mbar_init(&sm.link[i], 1);
         mbar_init(sm.issued, NW);
         for (int i = 0; i < PSLOTS; i++) {
             mbar_init(&sm.pfull[i], WPG); // written by the 4 warps of a group
@@ -116,8 +112,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         return;
     }
     const int ctid = threadIdx.x;
-    uint32_t cpar = 0, lpar = 0;
-    gemv_consume<WF, ST, TPK>(p, p.pro, p.epi, w, sm, cpar, lpar, ctid, true); // waits for the previous kernel itself
+    uint32_t cpar = 0;
+    gemv_consume<WF, ST, TPK>(p, p.pro, p.epi, w, sm, cpar, ctid, true); // waits for the previous kernel itself
     LLMRS_TRACE_FLUSH(0);
     if (ctid == 0)
         trace_end(p.trace, p.trace_slot);

@@ -44,7 +44,7 @@ __host__ __device__ constexpr int sbytes(int st) { return st == 0 ? 2 : 4; }
 __host__ __device__ constexpr size_t align_up(size_t x, size_t a) { return (x + a - 1) & ~(a - 1); }
 
 struct SmemLayout {
-    size_t stage_bytes, scale_off, act_off, acts_off, actc_off, tb_off, link_off, bar_off, red_off, total;
+    size_t stage_bytes, scale_off, act_off, acts_off, actc_off, tb_off, bar_off, red_off, total;
 };
 
 // bytes of the region that holds either the per-warp transpose buffers (one
@@ -66,85 +66,14 @@ __host__ __device__ inline SmemLayout smem_layout(int wf, int st, int K, int sta
     L.acts_off = L.act_off + (size_t)nb * 32;
     L.actc_off = align_up(L.acts_off + (size_t)nb * 4, 16);
     L.tb_off = align_up(L.actc_off + (size_t)nb * 4, 16);
-    L.link_off = L.tb_off + tb_region_bytes();
-    L.bar_off = align_up(L.link_off + (size_t)NW * RPW * 4, 16);
-    // full, empty, link, activation-issued, product full / empty, summers' argmax key
-    L.red_off = L.bar_off + (size_t)(2 * stages + NW + 1 + 2 * PSLOTS + 1) * 8;
+    L.bar_off = align_up(L.tb_off + tb_region_bytes(), 16);
+    // full, empty, activation-issued, product full / empty, summers' argmax key
+    L.red_off = L.bar_off + (size_t)(2 * stages + 1 + 2 * PSLOTS + 1) * 8;
     L.total = align_up(L.red_off + 16 * 4, 16) + 128; // + slack to align the base
     return L;
 }
 
 // ------------------------------------------------------------- activation
-// Quantise one 32-value block held by one thread (bit-exact Q8_0) and pack it
-// for the weight format: Q4 order puts the even elements of every 8 in words
-// 0-3 and the odd ones in words 4-7 (matching low / high nibbles), Q8 keeps
-// the natural order.
-template <int WF>
-__device__ __forceinline__ void quantize_pack(const float (&v)[32], uint32_t *dst_words, float *dst_s, int *dst_c)
-{
-    float amax = 0.0f;
-#pragma unroll
-    for (int i = 0; i < 32; i++)
-        amax = fmaxf(amax, fabsf(v[i]));
-    float scale = 0.0f, inv = 0.0f;
-    if (amax != 0.0f) {
-        scale = __fdiv_rn(amax, 127.0f);
-        inv = __fdiv_rn(1.0f, scale);
-    }
-    int q[32];
-    int sum = 0;
-#pragma unroll
-    for (int i = 0; i < 32; i++) {
-        float r = roundf(__fmul_rn(v[i], inv));
-        r = fminf(fmaxf(r, -127.0f), 127.0f);
-        q[i] = (amax == 0.0f || r != r) ? 0 : (int)r;
-        sum += q[i];
-    }
-    uint32_t w[8];
-#pragma unroll
-    for (int j = 0; j < 8; j++) {
-        uint32_t x = 0;
-#pragma unroll
-        for (int k = 0; k < 4; k++) {
-            const int e = WF == 0 ? (j < 4 ? 8 * j + 2 * k : 8 * (j - 4) + 2 * k + 1) : 4 * j + k;
-            x |= (uint32_t)(q[e] & 0xFF) << (8 * k);
-        }
-        w[j] = x;
-    }
-    reinterpret_cast<uint4 *>(dst_words)[0] = make_uint4(w[0], w[1], w[2], w[3]);
-    reinterpret_cast<uint4 *>(dst_words)[1] = make_uint4(w[4], w[5], w[6], w[7]);
-    *dst_s = scale;
-    *dst_c = WF == 0 ? -8 * sum : 0;
-}
-
-// 32 floats through L2 only (data other GPUs wrote into this GPU's memory)
-__device__ __forceinline__ void load32_cg(const float *src, float (&v)[32])
-{
-#pragma unroll
-    for (int j = 0; j < 8; j++) {
-        const float4 t = __ldcg(reinterpret_cast<const float4 *>(src) + j);
-        v[4 * j] = t.x;
-        v[4 * j + 1] = t.y;
-        v[4 * j + 2] = t.z;
-        v[4 * j + 3] = t.w;
-    }
-}
-
-// activations are written by other CTAs of the same persistent kernel: read
-// them through L2 (ld.global.cg), never from a possibly stale L1 line
-__device__ __forceinline__ void load32(const float *src, float (&v)[32])
-{
-    const float4 *s4 = reinterpret_cast<const float4 *>(src);
-#pragma unroll
-    for (int i = 0; i < 8; i++) {
-        const float4 f = __ldcg(s4 + i);
-        v[4 * i] = f.x;
-        v[4 * i + 1] = f.y;
-        v[4 * i + 2] = f.z;
-        v[4 * i + 3] = f.w;
-    }
-}
-
 // Fill the shared-memory activation (codes, scales, corrections).  One thread
 // per 32-block; `nthr` threads with ids `tid` take part; `bar` is a named
 // barrier id covering exactly those threads.
@@ -672,16 +601,14 @@ struct GemvSmem {
     size_t stage_bytes, scale_off;
     int S;                   // stages, a multiple of NG
     uint64_t *full, *empty;  // [S] each: filled by the producer / released by a warp group
-    uint64_t *link;          // [NW]: running-sum handoff between groups
     uint64_t *issued;        // activation requested (one-kernel path only; nullptr otherwise)
     uint64_t *pfull, *pempty; // [PSLOTS]: product slot written by a group / summed by a summer
     unsigned long long *sbest; // summers' best argmax key
     uint32_t *act;           // quantised activation, packed per block
     float *act_s;            // activation block scales
     int *act_c;              // per block: -8 * sum(q) (Q4 offset)
-    float *tbuf, *linkbuf, *red;
+    float *tbuf, *red;
     float *prod;             // [PSLOTS][TR][TBS] block products (aliases tbuf: a CTA uses one)
-    unsigned long long *ready_mark = nullptr; // optional: latest time a CTA finished the prologue
 };
 
 // This CTA's share of a GEMV: rows [r0, r1) in tiles of B rows.  TPS tile sets
@@ -720,7 +647,7 @@ __device__ __forceinline__ int gemv_group_iters(const GemvWork &w, int g)
 }
 
 // Parity of the number of times each ring stage is filled by one GEMV op of
-// this CTA (bit s), and of each warp's link arrivals (bit w).
+// this CTA (bit s).
 __device__ __forceinline__ uint32_t gemv_stage_use_parity(const GemvWork &w, int S)
 {
     const int spg = S / NG;
@@ -732,16 +659,6 @@ __device__ __forceinline__ uint32_t gemv_stage_use_parity(const GemvWork &w, int
             m |= (uint32_t)(uses & 1) << (g + NG * j);
         }
     }
-    return m;
-}
-
-__device__ __forceinline__ uint32_t gemv_link_parity(const GemvWork &w)
-{
-    if (w.GT == 1)
-        return 0;
-    uint32_t m = 0;
-    for (int warp = 0; warp < NW; warp++)
-        m |= (uint32_t)(gemv_group_iters(w, warp / WPG) & 1) << warp;
     return m;
 }
 
@@ -876,14 +793,13 @@ __device__ __forceinline__ void gemv_epilogue(const GemvParams &p, const int epi
 }
 
 // Consumers (the NW consumer warps, ctid = 0 .. NW*32-1): prologue, steps,
-// epilogue of one GEMV.  cpar / lpar: per stage, parity of the full-barrier
-// phase to wait for next; per warp, parity of its link arrivals so far (kept
-// across ops; advanced to the op's end on return).  dep_wait: the prologue
+// epilogue of one GEMV.  cpar: per stage, parity of the full-barrier phase to
+// wait for next (advanced to the op's end on return).  dep_wait: the prologue
 // waits for the previous kernel itself (after the loads that do not depend on
 // it); otherwise the caller has already waited for the op's input.
 template <int WF, int ST, bool TPK = false>
 __device__ __forceinline__ void gemv_consume(const GemvParams &p, const int pro, const int epi, const GemvWork &w,
-                                             const GemvSmem &sm, uint32_t &cpar, uint32_t &lpar, int ctid,
+                                             const GemvSmem &sm, uint32_t &cpar, int ctid,
                                              bool dep_wait = false)
 {
     constexpr int W_ROW = CB * wbytes_per_block(WF);
@@ -895,8 +811,6 @@ __device__ __forceinline__ void gemv_consume(const GemvParams &p, const int pro,
     named_bar_sync(1, PRO_THREADS);
     if (ctid == 0) {
         trace_ready(p.trace, p.trace_slot);
-        if (sm.ready_mark)
-            atomicMax(sm.ready_mark, (unsigned long long)globaltimer_ns());
     }
     LLMRS_TRACE_END(2);
 
@@ -1020,7 +934,6 @@ __device__ __forceinline__ void gemv_consume(const GemvParams &p, const int pro,
     }
     // every consumer thread advances the op-start parities identically
     cpar ^= gemv_stage_use_parity(w, sm.S);
-    lpar ^= gemv_link_parity(w);
     if (epi == EPI_ARGMAX) {
         // rows summed by the summer warps (groups sharing a tile) add their key
         named_bar_sync(2, PRO_THREADS + NSUM * 32);
